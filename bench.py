@@ -1,0 +1,453 @@
+"""Benchmark of the block-sparse attention forward path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c2|c3|c4|c5]
+
+Metric: effective TFLOP/s over LIVE mask elements,
+4 * D * live * B * H per forward, with ms per forward.  Default workload c2
+(configs[1]): dilated-4 mask, class A residue-4 permutation, 128x32 tiles,
+B1 H16 N8192 D128, bf16, ~N(0,1) synthetic inputs.
+
+One step = one pass of the hot path over one batch resident in HBM: the residue
+permutation of Q, K, V (one launch) and the block-sparse attention with LSE,
+whose epilogue writes O/LSE back in original row order (fused inverse
+permutation).  The block index and the forward's work list depend on the mask
+only; they are built once per mask (as the reference builds its BlockIndex
+offline) and their time is reported separately (``index_ms``).
+
+Multi-GPU (torchrun, one process per GPU): every rank runs the same workload on
+its own batch (weak scaling, no data-path collective); time is the max over
+ranks of the CUDA-event time of the K steps.  ``--impl reference`` times the CPU
+restatement of the reference's dense masked attention (gpu/reference.py) on the
+host cores instead.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: (B, H, N, D, mask spec name, residue stride, BQ, A, seed, description)
+    "c1": (1, 4, 1024, 64, "window-128", 0, 128, 32, 0,
+           "c1: window-128, B1 H4 N1024 D64 (fp32 inputs cast to bf16), 128x32 tiles"),
+    "c2": (1, 16, 8192, 128, "dilated-4", 4, 128, 32, 1,
+           "c2: dilated-4 + residue-perm-4, 128x32 tiles, B1 H16 N8192 D128 bf16"),
+    "c3": (2, 16, 16384, 128, "local64+str8", 8, 128, 32, 2,
+           "c3: local64+str8 + residue-perm-8, 128x32 tiles, B2 H16 N16384 D128 bf16"),
+    "c4": (4, 32, 8192, 128, "sinks4+win512", 0, 128, 32, 3,
+           "c4: sinks4+win512, 128x32 tiles, B4 H32 N8192 D128 bf16"),
+    "c5": (2, 64, 32768, 128, "local1024+str16", 16, 128, 32, 4,
+           "c5: window-1024 (identity, 128x128) + far1024+str16 (residue-perm-16, 128x32) "
+           "split + LSE merge, B2 H64 N32768 D128 bf16"),
+}
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained"), d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def _traffic_from_profiles(workload):
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / f"attn_fwd_{workload}.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln.strip() for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() in ("active", "1"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def live_flops(B, H, N, D, name):
+    from polyhedral_b200 import masks_gpu
+    live = masks_gpu.numpy_mask(name).live_count(N)
+    return 4.0 * D * live * B * H, live
+
+
+class Pipeline:
+    """Mask-only preprocessing plus the per-batch step of one workload."""
+
+    def __init__(self, wl, device):
+        import torch
+        from polyhedral_b200 import attention, blockindex, masks_gpu, permute, split
+        B, H, N, D, name, s, BQ, A, seed, _ = WORKLOADS[wl]
+        self.wl, self.B, self.H, self.N, self.D = wl, B, H, N, D
+        self.name, self.s, self.BQ, self.A = name, s, BQ, A
+        self.device = device
+        self.spec = masks_gpu.triton_params(name)
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        if wl == "c5":
+            self.split = split.SplitPlan(
+                [split.SplitPart(masks_gpu.numpy_mask("window-1024"), 128, 128, 0),
+                 split.SplitPart(masks_gpu.numpy_mask("far1024+str16"), BQ, A, s)], N, device)
+            self.perm = None
+            self.plan = None
+        else:
+            self.split = None
+            self.perm = permute.residue_perm_device(N, s, device) if s else None
+            dbi = blockindex.build_device(masks_gpu.numpy_mask(name), N, BQ, A,
+                                          perm_q=self.perm, perm_kv=self.perm, device=device)
+            self.plan = attention.make_plan(dbi.kv_idx, dbi.kv_num, dbi.kv_partial, N, BQ, A)
+            self.dbi = dbi
+        torch.cuda.synchronize(device)
+        self.index_ms = (time.perf_counter() - t0) * 1e3
+
+    def launches_per_step(self):
+        if self.split is not None:
+            return 1 + 1 + 1 + 1     # attention (window), gather, attention (lattice), merge
+        return 2 if self.perm is not None else 1
+
+    def step(self, q, k, v, o=None, lse=None):
+        from polyhedral_b200 import attention, permute
+        if self.split is not None:
+            return self.split.run(q, k, v)
+        if self.perm is not None:
+            q, k, v = permute.apply_perm_many((q, k, v), self.perm)
+        return attention.block_sparse_attention(
+            q, k, v, None, None, None, *self.spec, self.BQ, self.A, perm_q=self.perm,
+            perm_kv=self.perm, o_row_map=self.perm, plan=self.plan, return_lse=True,
+            out=o, lse_out=lse)
+
+    def attn_only(self, q, k, v, o, lse):
+        """The dominant kernel alone (inputs already in kernel order)."""
+        from polyhedral_b200 import attention
+        return attention.block_sparse_attention(
+            q, k, v, None, None, None, *self.spec, self.BQ, self.A, perm_q=self.perm,
+            perm_kv=self.perm, o_row_map=self.perm, plan=self.plan, return_lse=True,
+            out=o, lse_out=lse)
+
+
+def make_inputs(wl, device, seed_offset=0, generator_device="cuda"):
+    import torch
+    B, H, N, D, _, _, _, _, seed, _ = WORKLOADS[wl]
+    g = torch.Generator(device=device).manual_seed(seed + 1000 * seed_offset)
+    return [torch.randn(B * H, N, D, device=device, generator=g).bfloat16() for _ in range(3)]
+
+
+def run_ours(args, rank, world, device):
+    import torch
+    import torch.distributed as dist
+    wl = args.workload
+    B, H, N, D, name, s, BQ, A, seed, desc = WORKLOADS[wl]
+    flops, live = live_flops(B, H, N, D, name)
+    pipe = Pipeline(wl, device)
+
+    # inputs rotate over enough buffer sets that each step reads data not in L2
+    props = torch.cuda.get_device_properties(device)
+    l2 = getattr(props, "L2_cache_size", 0) or (126 << 20)
+    step_bytes = 4 * B * H * N * D * 2
+    nbuf = max(2, -(-2 * l2 // step_bytes) + 1)
+    bufs = [make_inputs(wl, device, rank * 64 + i) for i in range(nbuf)]
+    outs = [(torch.empty(B * H, N, D, device=device, dtype=torch.bfloat16),
+             torch.empty(B * H, N, device=device, dtype=torch.float32)) for _ in range(nbuf)]
+
+    def do_step(i):
+        q, k, v = bufs[i % nbuf]
+        o, lse = outs[i % nbuf]
+        if pipe.split is not None:
+            return pipe.step(q, k, v)
+        return pipe.step(q, k, v, o, lse)
+
+    for i in range(args.warmup):
+        do_step(i)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    st = pipe.plan.status() if pipe.plan is not None else 0
+    if st:
+        raise RuntimeError(f"attention kernel reported device status {st} during warm-up")
+
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for i in range(args.steps):
+            do_step(i)
+        ev1.record()
+        torch.cuda.synchronize(device)
+        t_ms = ev0.elapsed_time(ev1)
+        # keep the same load running (untimed) so the sampler sees >= 1 s of it
+        extra = int(max(0.0, 1000.0 - t_ms) / max(t_ms / args.steps, 1e-3))
+        for i in range(extra):
+            do_step(i)
+        torch.cuda.synchronize(device)
+    if world > 1:
+        t = torch.tensor([t_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms = float(t.item())
+        dist.barrier()
+    ms_per_step = t_ms / args.steps
+    value = flops * world / (ms_per_step * 1e-3) / 1e12
+
+    # dominant kernel alone, CUDA events on the launching stream
+    kernel_ms = None
+    if pipe.split is None:
+        from polyhedral_b200 import permute
+        kin = [permute.apply_perm_many(bufs[i], pipe.perm) if pipe.perm is not None else bufs[i]
+               for i in range(nbuf)]
+        torch.cuda.synchronize(device)
+        reps = max(args.steps, 20)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(3):
+            pipe.attn_only(*kin[i % nbuf], *outs[i % nbuf])
+        e0.record()
+        for i in range(reps):
+            pipe.attn_only(*kin[i % nbuf], *outs[i % nbuf])
+        e1.record()
+        torch.cuda.synchronize(device)
+        kernel_ms = e0.elapsed_time(e1) / reps
+        del kin
+
+    # end to end through the public API with host buffers (rank-local)
+    e2e = None
+    if rank == 0 or world > 1:
+        hq = [x.cpu().pin_memory() for x in bufs[0]]
+        ho = torch.empty(B * H, N, D, dtype=torch.bfloat16).pin_memory()
+        hl = torch.empty(B * H, N, dtype=torch.float32).pin_memory()
+        e2e_steps = max(5, min(args.steps, 50))
+        for i in range(2):
+            qd, kd, vd = (x.to(device, non_blocking=True) for x in hq)
+            o, lse = pipe.step(qd, kd, vd)
+            ho.copy_(o, non_blocking=True)
+            hl.copy_(lse, non_blocking=True)
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(e2e_steps):
+            qd, kd, vd = (x.to(device, non_blocking=True) for x in hq)
+            o, lse = pipe.step(qd, kd, vd)
+            ho.copy_(o, non_blocking=True)
+            hl.copy_(lse, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize(device)
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": round(flops * world / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+               "ms_per_step": round(e2e_ms, 4),
+               "h2d_bytes_per_step": 3 * B * H * N * D * 2,
+               "d2h_bytes_per_step": B * H * N * D * 2 + B * H * N * 4}
+
+    peak, peak_sus, hbm, peak_kind = _peaks()
+    roof = None
+    if kernel_ms is not None:
+        ach = flops / (kernel_ms * 1e-3) / 1e12
+        traffic = _traffic_from_profiles(wl)
+        roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(ach / peak, 4), "traffic": traffic,
+                "kernel": "attn_fwd_kernel", "kernel_ms": round(kernel_ms, 5),
+                "peak_source": f"{peak_kind} bf16 dense (burst)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(wl, budget_s=args.cpu_budget)
+
+    if rank == 0:
+        line = {
+            "metric": "block-sparse attn fwd live-element TFLOP/s & ms/fwd at 1/2/4/8 B200; % bf16 peak",
+            "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic ~N(0,1) (seeded), random inputs per rank",
+            "config": {"workload": desc, "global_batch": B * H * world, "seq_len": N,
+                       "head_dim": D, "parallelism": f"head-sharded x{world} (no collective)",
+                       "live_elements_per_head": live, "live_gflop_per_step_per_gpu": round(flops / 1e9, 3),
+                       "l2": f"inputs rotated over {nbuf} buffer sets ({nbuf * step_bytes >> 20} MiB >= 2x L2)",
+                       "index_ms": round(pipe.index_ms, 3),
+                       "step": "residue permutation of Q,K,V + attention (O, LSE) with fused inverse permutation"
+                               if wl != "c5" else "window part + gather + lattice part + LSE merge"},
+            "pct_bf16_peak": round(value / world / peak, 4),
+            "gpu_launches": pipe.launches_per_step() * args.steps,
+            "clocks": clk.summary(),
+            "e2e": e2e,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def _cpu_rows(wl, rows_idx, g, M):
+    """Oracle attention (CPU restatement of gpu/reference.py) for the query rows
+    `rows_idx` of one head against all N keys; returns (live elements, seconds)."""
+    import torch
+    import oracle as O
+    B, H, N, D, *_ = WORKLOADS[wl]
+    q = torch.randn(1, len(rows_idx), D, generator=g)
+    k, v = (torch.randn(1, N, D, generator=g) for _ in range(2))
+    Mr = M[torch.as_tensor(rows_idx)]
+    t0 = time.perf_counter()
+    O.attention(q, k, v, Mr)
+    return int(Mr.sum()), time.perf_counter() - t0
+
+
+def cpu_baseline(wl, budget_s=12.0, threads=None, rows=1024, start=0):
+    """The oracle on the host cores, `rows` query rows per piece spread evenly
+    over the sequence (so the live fraction is the workload's), until ~budget_s
+    seconds of compute; TFLOP/s over the live elements done."""
+    import numpy as np
+    import torch
+    import oracle as O
+    from polyhedral_b200 import masks_gpu
+    B, H, N, D, name, _, _, _, seed, _ = WORKLOADS[wl]
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    M = torch.from_numpy(O.dense_mask(*masks_gpu.triton_params(name), N))
+    g = torch.Generator().manual_seed(seed + start)
+    rows = min(rows, N)
+    stride = N // rows
+    live, dt, done = 0, 0.0, 0
+    while True:
+        idx = np.arange(rows) * stride + ((start + done) % stride)
+        lv, t = _cpu_rows(wl, idx, g, M)
+        live += lv
+        dt += t
+        done += 1
+        if dt >= budget_s or done >= stride * B * H:
+            break
+    val = 4.0 * D * live / dt / 1e12
+    return {"value": round(val, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{done} x {rows} query rows (evenly spaced) x {N} keys of {wl}, fp32 "
+                      f"dense masked attention (gpu/reference.py semantics), {dt:.2f} s",
+            "live_elements": live, "seconds": round(dt, 3)}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    wl = args.workload
+    B, H, N, D, name, *_ = WORKLOADS[wl]
+    flops, live = live_flops(B, H, N, D, name)
+    for i in range(args.warmup):
+        cpu_baseline(wl, budget_s=0.0, rows=256, start=i)
+    tot_live, tot_s = 0, 0.0
+    for i in range(args.steps):
+        cb = cpu_baseline(wl, budget_s=0.0, rows=256, start=i)
+        tot_live += cb["live_elements"]
+        tot_s += cb["seconds"]
+    val = 4.0 * D * tot_live / tot_s / 1e12
+    ms = flops / (val * 1e12) * 1e3        # one whole forward at that rate
+    line = {
+        "impl": "reference",
+        "metric": "block-sparse attn fwd live-element TFLOP/s & ms/fwd at 1/2/4/8 B200; % bf16 peak",
+        "value": round(val, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic ~N(0,1)",
+        "config": {"workload": WORKLOADS[wl][9], "global_batch": B * H, "seq_len": N,
+                   "note": "each step times 256 evenly spaced query rows x N keys of one head; "
+                           "ms_per_step extrapolates to one whole forward"},
+        "cpu_baseline": {"value": round(val, 6), "unit": "TFLOP/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"256 evenly spaced query rows x {N} keys per step ({args.steps} steps), "
+                                   "dense fp32 masked attention (gpu/reference.py semantics)"},
+        "e2e": {"value": round(val, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device,
+                                timeout=datetime.timedelta(seconds=120))
+    try:
+        run_ours(args, rank, world, device)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

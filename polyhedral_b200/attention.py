@@ -1,0 +1,160 @@
+"""Block-sparse attention forward on sm_100a -- the drop-in for the reference's
+``block_sparse_attention`` (gpu/triton_attn.py:185-241).
+
+Same arguments, defaults and checks as the reference: q, k, v are [BH, N, D]
+with a contiguous last dimension; ``kv_idx`` / ``kv_num`` / ``kv_partial`` come
+from ``blockindex``; ``perm_q`` / ``perm_kv`` (permuted position -> original index)
+say where the physically permuted rows came from, so the predicate is evaluated in
+original coordinates; ``perm_kv`` defaults to ``perm_q``.  The kernel is the
+tcgen05/TMEM one in csrc/attn.cu; there is no other implementation.
+
+Extensions (keyword-only): ``return_lse`` returns (o, lse) with lse [BH, N] fp32
+(natural log, -inf for a row with no live key); ``o_row_map`` writes row r of the
+result at ``o_row_map[r]`` (pass ``perm_q`` to get O back in original order, fusing
+the inverse permutation); ``plan`` reuses a work list built once by ``make_plan``;
+``out`` / ``lse_out`` supply output buffers; ``check`` synchronises and raises if
+the kernel reported a device-side failure.  The reference's class-B emulation
+knobs (``gather_kv``, ``gather_mult``, ``gather_scatter``) are rejected when set;
+``num_warps`` / ``num_stages`` are accepted and ignored.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+CAUSAL, WINDOW, DILATED, LOCAL_STRIDED, TWOBAND, SINKS, FAR_STRIDED = range(7)
+
+_DTYPES = {torch.bfloat16: _lib.PA_BF16, torch.float16: _lib.PA_F16}
+
+
+class AttnPlan:
+    """Device work list for one block index (``pa_attn_plan``): the per-256-row
+    union of listed tiles with each 128-row half's dead/full/partial status,
+    ordered longest first.  Reusable by every forward on the same index."""
+
+    def __init__(self, kv_idx, kv_num, kv_partial, N, BQ, A, device=None):
+        device = device or kv_num.device
+        self.N, self.BQ, self.A = int(N), int(BQ), int(A)
+        self.kv_idx, self.kv_num, self.kv_partial = kv_idx, kv_num, kv_partial
+        self.kv_stride = int(kv_idx.shape[1]) if kv_idx.dim() == 2 else 0
+        a = _args_skeleton(N, BQ, A, kv_idx, kv_num, kv_partial, self.kv_stride)
+        nbytes = _lib.load().pa_attn_workspace_size(ctypes.byref(a))
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _lib.call("pa_attn_plan", ctypes.byref(a), self.workspace.data_ptr(), nbytes,
+                  _lib.stream_handle(device))
+
+    def status(self):
+        """0 if the last forward on this plan finished cleanly (synchronises)."""
+        st = _lib.c_i32(0)
+        lib = _lib.load()
+        lib.pa_attn_status(self.workspace.data_ptr(), ctypes.byref(st),
+                           _lib.stream_handle(self.workspace.device))
+        return int(st.value)
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def _args_skeleton(N, BQ, A, kv_idx, kv_num, kv_partial, kv_stride):
+    a = _lib.PaAttnArgs()
+    a.N, a.BQ, a.A = int(N), int(BQ), int(A)
+    a.BH, a.D, a.dtype = 1, 128, _lib.PA_BF16
+    a.kv_idx = _ptr(kv_idx) if kv_stride else None
+    a.kv_num = _ptr(kv_num)
+    a.kv_partial = _ptr(kv_partial) if kv_stride else None
+    a.kv_stride = int(kv_stride)
+    # placeholders: the plan reads only the block index
+    a.q = a.k = a.v = a.o = _ptr(kv_num)
+    return a
+
+
+def make_plan(kv_idx, kv_num, kv_partial, N, BQ, A):
+    """Build the forward's work list once for a block index."""
+    return AttnPlan(_index_tensor(kv_idx, torch.int32, kv_num.device),
+                    _index_tensor(kv_num, torch.int32, kv_num.device),
+                    _index_tensor(kv_partial, torch.int8, kv_num.device), N, BQ, A)
+
+
+def _index_tensor(t, dtype, device):
+    t = torch.as_tensor(t)
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    return t.to(device).contiguous()
+
+
+def _perm(p, N, device):
+    if p is None:
+        return None
+    t = torch.as_tensor(p)
+    if t.numel() != N:
+        raise ValueError(f"permutation has {t.numel()} entries, expected N={N}")
+    return t.to(device=device, dtype=torch.int32).contiguous()
+
+
+def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
+                           kind, p0, p1, p2, BQ, A, scale=None,
+                           perm_q=None, perm_kv=None, gather_kv=False,
+                           gather_mult=1, gather_scatter=True,
+                           num_warps=4, num_stages=2, *, return_lse=False,
+                           o_row_map=None, plan=None, out=None, lse_out=None,
+                           check=False):
+    """q, k, v: [BH, N, D] (bf16 or fp16, D in {64, 128}), on one CUDA device.
+    Returns o [BH, N, D] (same dtype), or (o, lse) with ``return_lse``."""
+    if gather_kv or gather_mult != 1:
+        raise NotImplementedError(
+            "gather_kv / gather_mult emulate class-B traffic in the reference "
+            "(gpu/triton_attn.py:99-128); they are not part of this kernel")
+    BH, N, D = q.shape
+    assert N % BQ == 0 and N % A == 0, "cost model and kernel both assume this"
+    assert k.shape == v.shape == q.shape
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("block_sparse_attention runs on the GPU only")
+    if q.dtype not in _DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError(f"q/k/v must share dtype bf16 or fp16, got {q.dtype}/{k.dtype}/{v.dtype}")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.stride(2) != 1:
+            raise ValueError(f"{name}: last dimension must be contiguous")
+    dev = q.device
+    pq = _perm(perm_q, N, dev)
+    pk = _perm(perm_kv, N, dev) if perm_kv is not None else pq
+    rmap = _perm(o_row_map, N, dev)
+
+    if plan is None:
+        plan = make_plan(kv_idx, kv_num, kv_partial, N, BQ, A)
+    elif (plan.N, plan.BQ, plan.A) != (N, BQ, A):
+        raise ValueError("plan was built for a different (N, BQ, A)")
+
+    o = out if out is not None else torch.empty((BH, N, D), dtype=q.dtype, device=dev)
+    lse = None
+    if return_lse:
+        lse = lse_out if lse_out is not None else torch.empty((BH, N), dtype=torch.float32,
+                                                              device=dev)
+
+    a = _lib.PaAttnArgs()
+    a.q, a.k, a.v, a.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    a.lse = _ptr(lse)
+    a.BH, a.N, a.D, a.dtype = BH, N, D, _DTYPES[q.dtype]
+    a.q_bh_stride, a.q_row_stride = q.stride(0), q.stride(1)
+    a.k_bh_stride, a.k_row_stride = k.stride(0), k.stride(1)
+    a.v_bh_stride, a.v_row_stride = v.stride(0), v.stride(1)
+    a.o_bh_stride, a.o_row_stride = o.stride(0), o.stride(1)
+    a.lse_bh_stride = lse.stride(0) if lse is not None else 0
+    a.kv_idx = _ptr(plan.kv_idx) if plan.kv_stride else None
+    a.kv_num = _ptr(plan.kv_num)
+    a.kv_partial = _ptr(plan.kv_partial) if plan.kv_stride else None
+    a.kv_stride = plan.kv_stride
+    a.BQ, a.A = BQ, A
+    a.perm_q, a.perm_kv, a.o_row_map = _ptr(pq), _ptr(pk), _ptr(rmap)
+    a.pred = _lib.PaPred(int(kind), int(p0), int(p1), int(p2))
+    a.scale = float(scale) if scale else 0.0
+    ws = plan.workspace
+    _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
+              _lib.stream_handle(dev))
+    if check:
+        st = plan.status()
+        if st:
+            raise _lib.PolyattnError("pa_attn_fwd", _lib.PA_ERR_DEVICE,
+                                     f"device status {st} (a bounded wait ran out)")
+    return (o, lse) if return_lse else o

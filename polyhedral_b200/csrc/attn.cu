@@ -1,0 +1,884 @@
+// Block-sparse flash-attention forward for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Replaces the reference's Triton kernel (gpu/triton_attn.py:62-182) and its
+// launcher (:185-241) with the same semantics: per query row, online softmax over
+// the KV tiles the block index lists; the mask predicate is evaluated in
+// original coordinates (perm_q[i] - perm_kv[j]) on partial tiles only; a row with
+// no live key yields O = 0.  In addition it writes LSE (natural log, -inf for a
+// dead row).
+//
+// Work decomposition.  A CTA owns 256 query rows of one (batch, head) at a time
+// as two 128-row halves that share one stream of 128-row KV "super-tiles": the
+// plan kernel merges the two halves' tile lists into one ascending union and
+// records, per tile and half, whether the tile is dead, full or partial for that
+// half.  A super-tile is made of 128/L segments of L = min(A, 128) KV rows, each
+// fetched by its own TMA box, so KV tiles of 16/32/64 rows are gathered at tile
+// granularity while every MMA runs at N = 128.  Segments past the end of the list
+// are fetched from row N (out of bounds, zero-filled) and masked.
+//
+// Warp roles (320 threads):
+//   warps 0-3  softmax, half 0 (TMEM lanes 0-127)    warps 4-7  softmax, half 1
+//   warp 8     TMA producer (Q tiles, K/V ring)      warp 9     MMA issuer, TMEM owner
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D).
+// P (16-bit) is written by the softmax warps into columns [64,128) of its S buffer
+// and consumed from TMEM by the P.V MMA.  Per KV super-tile j the MMA warp issues,
+// for each half h in turn, PV_h(j-1) then S_h(j); tcgen05 ops of one thread
+// complete in order, so the commit that publishes S_h(j) also proves PV_h(j-1)
+// complete, which is what lets the softmax warps rescale O_h in place.
+//
+// Every wait on a barrier is bounded (common.cuh mbar_wait): on expiry the CTA
+// records a status in the workspace, stops issuing work, drains what it issued and
+// frees TMEM before exiting.
+#include <cuda.h>
+#include <math.h>
+#include <mutex>
+#include "common.cuh"
+#include "capi_util.h"
+
+namespace pa {
+namespace {
+
+constexpr int kThreads = 320;
+constexpr int kLoadWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int BM = 128;   // query rows per half
+constexpr int BN = 128;   // KV rows per super-tile
+constexpr int kTmemCols = 512;
+constexpr uint32_t kDrainLimitNs = 200u * 1000u * 1000u;
+
+// ----------------------------------------------------------------- plan layout
+struct PlanView {
+  int32_t* err;        // status word
+  int32_t* pair_cnt;   // [npairs] union entries of pair p
+  int32_t* order;      // [npairs] pairs sorted by decreasing entry count
+  int32_t* entries;    // [npairs * cap] ascending A-tile ids
+  uint8_t* status;     // [npairs * cap] bits 0-1 half 0, bits 2-3 half 1: 0 dead 1 full 2 partial
+  int cap;
+  int npairs;
+};
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct PlanSizes {
+  size_t off_cnt, off_order, off_entries, off_status, total;
+  int cap, npairs;
+};
+
+PlanSizes plan_sizes(int N, int A) {
+  PlanSizes s;
+  s.npairs = (N + 2 * BM - 1) / (2 * BM);
+  s.cap = N / A;
+  s.off_cnt = 256;
+  s.off_order = align_up(s.off_cnt + 4ull * s.npairs, 256);
+  s.off_entries = align_up(s.off_order + 4ull * s.npairs, 256);
+  s.off_status = align_up(s.off_entries + 4ull * s.npairs * s.cap, 256);
+  s.total = align_up(s.off_status + (size_t)s.npairs * s.cap, 256);
+  return s;
+}
+
+PlanView plan_view(void* ws, int N, int A) {
+  const PlanSizes s = plan_sizes(N, A);
+  char* b = static_cast<char*>(ws);
+  return PlanView{reinterpret_cast<int32_t*>(b), reinterpret_cast<int32_t*>(b + s.off_cnt),
+                  reinterpret_cast<int32_t*>(b + s.off_order),
+                  reinterpret_cast<int32_t*>(b + s.off_entries),
+                  reinterpret_cast<uint8_t*>(b + s.off_status), s.cap, s.npairs};
+}
+
+// ------------------------------------------------------------- plan kernels
+constexpr int kPlanThreads = 256;
+
+// One CTA per 256-row pair: union of the listed tiles of the query blocks that
+// cover each 128-row half, with each half's status.  A tile is full for a half
+// when every covering block lists it as full, dead when no covering block lists
+// it, partial otherwise (the predicate then decides element by element).
+__global__ void __launch_bounds__(kPlanThreads)
+plan_pairs_kernel(const int32_t* __restrict__ kv_idx, const int32_t* __restrict__ kv_num,
+                  const int8_t* __restrict__ kv_partial, int kv_stride, int N, int BQ,
+                  PlanView pv) {
+  extern __shared__ uint8_t cnt[];   // [4][cap]: present h0, full h0, present h1, full h1
+  __shared__ int s_warp[kPlanThreads / 32];
+  const int cap = pv.cap;
+  const int p = blockIdx.x;
+  for (int t = threadIdx.x; t < 4 * cap; t += kPlanThreads) cnt[t] = 0;
+  __syncthreads();
+  int nblk[2] = {0, 0};
+  for (int h = 0; h < 2; ++h) {
+    const int r0 = p * 2 * BM + h * BM;
+    if (r0 >= N) continue;
+    const int r1 = min(r0 + BM, N);
+    const int b0 = r0 / BQ, b1 = (r1 - 1) / BQ;
+    nblk[h] = b1 - b0 + 1;
+    uint8_t* pres = cnt + (2 * h) * cap;
+    uint8_t* full = cnt + (2 * h + 1) * cap;
+    for (int b = b0; b <= b1; ++b) {
+      const int n = kv_num[b];
+      for (int e = threadIdx.x; e < n; e += kPlanThreads) {
+        const int t = kv_idx[(size_t)b * kv_stride + e];
+        if ((unsigned)t < (unsigned)cap) {
+          pres[t] += 1;
+          full[t] += kv_partial[(size_t)b * kv_stride + e] == 0 ? 1 : 0;
+        }
+      }
+      __syncthreads();   // one block at a time: a tile appears at most once per block
+    }
+  }
+  // ascending compaction of tiles live in either half
+  const int chunk = (cap + kPlanThreads - 1) / kPlanThreads;
+  const int t0 = min(cap, (int)threadIdx.x * chunk), t1 = min(cap, t0 + chunk);
+  auto status_of = [&](int t) -> int {
+    int st = 0;
+    for (int h = 0; h < 2; ++h) {
+      const int pr = cnt[(2 * h) * cap + t], fu = cnt[(2 * h + 1) * cap + t];
+      const int s = (nblk[h] == 0 || pr == 0) ? 0 : (fu == nblk[h] ? 1 : 2);
+      st |= s << (2 * h);
+    }
+    return st;
+  };
+  int mine = 0;
+  for (int t = t0; t < t1; ++t) mine += status_of(t) != 0;
+  // block exclusive scan
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = mine;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < kPlanThreads / 32 ? s_warp[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kPlanThreads / 32) s_warp[lane] = w;
+  }
+  __syncthreads();
+  int pos = (warp ? s_warp[warp - 1] : 0) + x - mine;
+  const int total = s_warp[kPlanThreads / 32 - 1];
+  int32_t* ent = pv.entries + (size_t)p * cap;
+  uint8_t* sts = pv.status + (size_t)p * cap;
+  for (int t = t0; t < t1; ++t) {
+    const int st = status_of(t);
+    if (st) {
+      ent[pos] = t;
+      sts[pos] = (uint8_t)st;
+      ++pos;
+    }
+  }
+  if (threadIdx.x == 0) pv.pair_cnt[p] = total;
+}
+
+// Longest-first order of the pairs (stable on ties), for the static schedule.
+__global__ void plan_order_kernel(PlanView pv) {
+  const int n = pv.npairs;
+  for (int p = threadIdx.x; p < n; p += blockDim.x) {
+    const int c = pv.pair_cnt[p];
+    int rank = 0;
+    for (int q = 0; q < n; ++q) {
+      const int d = pv.pair_cnt[q];
+      rank += (d > c) || (d == c && q < p);
+    }
+    pv.order[rank] = p;
+  }
+  if (threadIdx.x == 0) *pv.err = 0;   // a new plan starts with a clean status
+}
+
+// ------------------------------------------------------------- forward kernel
+struct FwdParams {
+  int BH, N, A;
+  const int32_t* perm_q;
+  const int32_t* perm_kv;
+  const int32_t* o_row_map;
+  void* o;
+  float* lse;
+  long long o_bh_stride, o_row_stride, lse_bh_stride;
+  Pred pred;
+  float scale_log2;
+  PlanView pv;
+  uint32_t idesc_qk, idesc_pv;
+  int total_items;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int kTileBytes = BM * D * 2;               // one 128-row tile, 16-bit
+  static constexpr int kSlots = D == 128 ? 4 : 8;
+  static constexpr int kQOff = 0;
+  static constexpr int kKVOff = 2 * kTileBytes;
+  static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
+  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] drain kv_full[S] kv_empty[S]
+  static constexpr int kNumBars = 11 + 2 * kSlots;
+  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort flag
+  static constexpr int kColOff = (kMiscOff + 16 + 15) & ~15;  // per-warp column coords [8][128]
+  static constexpr int kBytes = kColOff + 8 * 128 * 4;
+  static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kBf16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Number of super-tiles of pair `p` and, for segment `sg` of super-tile `u`, the
+// first KV row (N when past the end) and the 4-bit status.
+struct SegInfo {
+  int row0;
+  int st;
+};
+
+template <int L>
+__device__ __forceinline__ int num_super(const FwdParams& P, int cnt) {
+  constexpr int S = BN / L;
+  if (P.A <= BN) return (cnt + S - 1) / S;
+  return cnt * (P.A / BN);
+}
+
+template <int L>
+__device__ __forceinline__ SegInfo seg_info(const FwdParams& P, const int32_t* ent,
+                                            const uint8_t* sts, int cnt, int u, int sg) {
+  constexpr int S = BN / L;
+  if (P.A <= BN) {
+    const int e = u * S + sg;
+    if (e < cnt) return SegInfo{__ldg(ent + e) * P.A, (int)__ldg(sts + e)};
+    return SegInfo{P.N, 0};
+  }
+  const int sub = P.A / BN;
+  const int e = u / sub;
+  return SegInfo{__ldg(ent + e) * P.A + (u - e * sub) * BN, (int)__ldg(sts + e)};
+}
+
+// Live bits of columns [32k, 32k + 32) of super-tile row `irow` (original row
+// index): bit c set when column 32k + c is live.  Dead segments give 0, full
+// segments all ones, partial segments evaluate the predicate per element
+// (`cols` holds original column indices when K/V rows are permuted).
+template <int L>
+__device__ __forceinline__ uint32_t chunk_mask(const Pred& pred, int k, const SegInfo* si,
+                                               int irow, const int* cols) {
+  if constexpr (L >= 32) {
+    constexpr int per = L / 32;
+    const SegInfo g = si[k / per];
+    if (g.st == 0) return 0u;
+    if (g.st == 1) return 0xffffffffu;
+    const int cbase = (k % per) * 32;
+    uint32_t w = 0;
+#pragma unroll 1
+    for (int c = 0; c < 32; ++c) {
+      const int j = cols ? cols[k * 32 + c] : g.row0 + cbase + c;
+      w |= (uint32_t)pred_live(pred, irow, j) << c;
+    }
+    return w;
+  } else {
+    uint32_t w = 0;
+#pragma unroll
+    for (int hw = 0; hw < 2; ++hw) {
+      const SegInfo g = si[2 * k + hw];
+      uint32_t b = 0;
+      if (g.st == 1) {
+        b = 0xffffu;
+      } else if (g.st == 2) {
+#pragma unroll 1
+        for (int c = 0; c < 16; ++c) {
+          const int j = cols ? cols[k * 32 + hw * 16 + c] : g.row0 + c;
+          b |= (uint32_t)pred_live(pred, irow, j) << c;
+        }
+      }
+      w |= b << (16 * hw);
+    }
+    return w;
+  }
+}
+
+template <int D, int L, bool kBf16>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const FwdParams P) {
+  using SM = Smem<D>;
+  constexpr int S = BN / L;              // segments per super-tile
+  constexpr int NS = SM::kSlots;
+  constexpr int kChunks = D / 64;        // 128-byte swizzle chunks along D
+  constexpr uint32_t kRegion = BM * 128; // bytes of one 64-column chunk of a 128-row tile
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem + SM::kQOff;
+  uint8_t* sKV = smem + SM::kKVOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 2;
+  uint64_t* s_full = bars + 4;
+  uint64_t* p_full = bars + 6;
+  uint64_t* o_full = bars + 8;
+  uint64_t* drain = bars + 10;
+  uint64_t* kv_full = bars + 11;
+  uint64_t* kv_empty = bars + 11 + NS;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
+  int* colbuf = reinterpret_cast<int*>(smem + SM::kColOff);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* err = P.pv.err;
+
+  if (threadIdx.x == 0) {
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&q_full[h], 1);
+      mbar_init(&q_empty[h], 1);
+      mbar_init(&s_full[h], 1);
+      mbar_init(&p_full[h], BM);
+      mbar_init(&o_full[h], 1);
+    }
+    mbar_init(drain, 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  const int npairs = P.pv.npairs;
+
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int qi = 0;
+      int q_armed[2] = {0, 0};
+      uint32_t kv_g = 0;
+      for (int it = blockIdx.x; it < P.total_items && !*s_abort; it += gridDim.x) {
+        const int bh = it / npairs;
+        const int p = __ldg(P.pv.order + (it - bh * npairs));
+        const int cnt = __ldg(P.pv.pair_cnt + p);
+        const int nsup = num_super<L>(P, cnt);
+        if (nsup == 0) continue;
+        const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
+        const uint8_t* sts = P.pv.status + (size_t)p * P.pv.cap;
+        bool ok = true;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (qi > 0) ok = mbar_wait(&q_empty[h], (qi - 1) & 1, s_abort, err, DEV_TIMEOUT_Q);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&q_full[h], SM::kTileBytes);
+          ++q_armed[h];
+          for (int c = 0; c < kChunks; ++c)
+            tma_load_3d(sQ + h * SM::kTileBytes + c * kRegion, &tm_q, &q_full[h], c * 64,
+                        p * 2 * BM + h * BM, bh);
+        }
+        if (!ok) break;
+        for (int u = 0; u < nsup && ok; ++u) {
+          SegInfo si[S];
+#pragma unroll
+          for (int sg = 0; sg < S; ++sg) si[sg] = seg_info<L>(P, ent, sts, cnt, u, sg);
+          for (int kv = 0; kv < 2; ++kv) {
+            const uint32_t slot = kv_g % NS;
+            if (kv_g >= (uint32_t)NS) {
+              ok = mbar_wait(&kv_empty[slot], ((kv_g / NS) - 1) & 1, s_abort, err,
+                             DEV_TIMEOUT_KV);
+              if (!ok) break;
+            }
+            ++kv_g;
+            uint8_t* dst = sKV + slot * SM::kTileBytes;
+            mbar_arrive_expect_tx(&kv_full[slot], SM::kTileBytes);
+            const void* tm = kv == 0 ? (const void*)&tm_k : (const void*)&tm_v;
+#pragma unroll
+            for (int sg = 0; sg < S; ++sg)
+              for (int c = 0; c < kChunks; ++c)
+                tma_load_3d(dst + c * kRegion + sg * L * 128, tm, &kv_full[slot], c * 64,
+                            si[sg].row0, bh);
+          }
+        }
+        ++qi;
+      }
+      // Teardown: let every copy this thread issued land before the CTA can exit.
+      // A phase that completed long ago also satisfies the parity test, so this
+      // only ever waits on copies still in flight.
+      const uint64_t t0 = globaltimer();
+      for (uint32_t s = 0; s < (uint32_t)NS && s < kv_g; ++s) {
+        const uint32_t uses = (kv_g - s + NS - 1) / NS;   // loads issued into slot s
+        while (!mbar_try_wait(&kv_full[s], (uses - 1) & 1)) {
+          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+        }
+      }
+      for (int h = 0; h < 2; ++h) {
+        if (q_armed[h] == 0) continue;
+        while (!mbar_try_wait(&q_full[h], (q_armed[h] - 1) & 1)) {
+          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int qi = 0;
+      uint32_t kv_c = 0;
+      uint32_t tp[2] = {0, 0};
+      bool ok = true;
+      const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
+      auto wait_kv = [&](uint32_t& slot) -> bool {
+        slot = kv_c % NS;
+        const bool r = mbar_wait(&kv_full[slot], (kv_c / NS) & 1, s_abort, err, DEV_TIMEOUT_KV);
+        ++kv_c;
+        tc_fence_after();
+        return r;
+      };
+      auto issue_s = [&](int h, uint32_t kslot) {
+        const uint32_t d = tmem + h * 128;
+        const uint32_t qa = sQa + h * SM::kTileBytes, ka = sKVa + kslot * SM::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kRegion + (kk & 3) * 32;
+          mma_ss(d, smem_desc_sw128(qa + off, 16), smem_desc_sw128(ka + off, 16), P.idesc_qk,
+                 kk > 0);
+        }
+      };
+      auto issue_pv = [&](int h, uint32_t vslot, bool acc) {
+        const uint32_t d = tmem + 256 + h * D;
+        const uint32_t pa_ = tmem + h * 128 + 64;
+        const uint32_t va = sKVa + vslot * SM::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ts(d, pa_ + kk * 8, smem_desc_sw128(va + kk * 16 * 128, kRegion), P.idesc_pv,
+                 (acc || kk > 0) ? 1u : 0u);
+      };
+      auto wait_p = [&](int h) -> bool {
+        const bool r = mbar_wait(&p_full[h], tp[h] & 1, s_abort, err, DEV_TIMEOUT_P);
+        ++tp[h];
+        tc_fence_after();
+        return r;
+      };
+      for (int it = blockIdx.x; it < P.total_items && ok; it += gridDim.x) {
+        const int bh = it / npairs;
+        const int p = __ldg(P.pv.order + (it - bh * npairs));
+        const int nsup = num_super<L>(P, __ldg(P.pv.pair_cnt + p));
+        if (nsup == 0) continue;
+        ok = mbar_wait(&q_full[0], qi & 1, s_abort, err, DEV_TIMEOUT_Q) &&
+             mbar_wait(&q_full[1], qi & 1, s_abort, err, DEV_TIMEOUT_Q);
+        tc_fence_after();
+        if (!ok) break;
+        uint32_t ks, vs;
+        if (!(ok = wait_kv(ks))) break;
+        issue_s(0, ks);
+        tc_commit(&s_full[0]);
+        issue_s(1, ks);
+        tc_commit(&s_full[1]);
+        tc_commit(&kv_empty[ks]);
+        for (int u = 1; u < nsup && ok; ++u) {
+          if (!(ok = wait_kv(vs))) break;
+          if (!(ok = wait_kv(ks))) break;
+          for (int h = 0; h < 2 && ok; ++h) {
+            if (!(ok = wait_p(h))) break;
+            issue_pv(h, vs, u > 1);
+            issue_s(h, ks);
+            tc_commit(&s_full[h]);
+          }
+          tc_commit(&kv_empty[vs]);
+          tc_commit(&kv_empty[ks]);
+        }
+        if (!ok) break;
+        tc_commit(&q_empty[0]);
+        tc_commit(&q_empty[1]);
+        if (!(ok = wait_kv(vs))) break;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!(ok = wait_p(h))) break;
+          issue_pv(h, vs, nsup > 1);
+          tc_commit(&o_full[h]);
+        }
+        tc_commit(&kv_empty[vs]);
+        ++qi;
+      }
+      // drain: the commit lands once every MMA issued above has completed
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int h = warp >> 2;              // which half
+    const int wq = warp & 3;              // TMEM lane quarter
+    const int r_in = wq * 32 + lane;      // row within the half
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + h * 128;
+    const uint32_t tO = tmem + lane_off + 256 + h * D;
+    int* mycols = colbuf + warp * 128;
+    uint32_t ts = 0, to = 0;
+    const float c2 = P.scale_log2;
+    for (int it = blockIdx.x; it < P.total_items; it += gridDim.x) {
+      const int bh = it / npairs;
+      const int p = __ldg(P.pv.order + (it - bh * npairs));
+      const int cnt = __ldg(P.pv.pair_cnt + p);
+      const int nsup = num_super<L>(P, cnt);
+      const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
+      const uint8_t* sts = P.pv.status + (size_t)p * P.pv.cap;
+      const int row = p * 2 * BM + h * BM + r_in;
+      const bool valid = row < P.N;
+      const int irow = valid ? (P.perm_q ? __ldg(P.perm_q + row) : row) : -(1 << 30);
+      float m_used = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int u = 0; u < nsup; ++u) {
+        SegInfo si[S];
+        int any_partial = 0;
+#pragma unroll
+        for (int sg = 0; sg < S; ++sg) {
+          si[sg] = seg_info<L>(P, ent, sts, cnt, u, sg);
+          si[sg].st = (si[sg].st >> (2 * h)) & 3;
+          any_partial |= si[sg].st == 2;
+        }
+        if (any_partial && P.perm_kv) {
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int c = k * 32 + lane;
+            const int sg = c / L;
+            int j = -1;
+#pragma unroll
+            for (int q = 0; q < S; ++q)
+              if (q == sg && si[q].st == 2) j = __ldg(P.perm_kv + si[q].row0 + (c - q * L));
+            mycols[c] = j;
+          }
+          __syncwarp();
+        }
+        // live bits of this row for the 128 columns, computed while S is in flight
+        uint32_t mk[4];
+        {
+          const int* cols = (any_partial && P.perm_kv) ? mycols : nullptr;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mk[k] = chunk_mask<L>(P.pred, k, si, irow, cols);
+        }
+        ok = mbar_wait(&s_full[h], ts & 1, s_abort, err, DEV_TIMEOUT_S);
+        ++ts;
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        float s[128];
+        {
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(tS + 0, r0);
+          tmem_ld32(tS + 32, r1);
+          tmem_ld32(tS + 64, r2);
+          tmem_ld32(tS + 96, r3);
+          tmem_wait_ld();
+          tmem_regs_ready(r0);
+          tmem_regs_ready(r1);
+          tmem_regs_ready(r2);
+          tmem_regs_ready(r3);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s[i] = __uint_as_float(r0[i]);
+            s[32 + i] = __uint_as_float(r1[i]);
+            s[64 + i] = __uint_as_float(r2[i]);
+            s[96 + i] = __uint_as_float(r3[i]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (mk[k] != 0xffffffffu) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (!((mk[k] >> i) & 1u)) s[k * 32 + i] = -INFINITY;
+          }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
+        const float m_tile = mx * c2;
+        const float m_new = fmaxf(m_used, m_tile);
+        bool bump = false;
+        float factor = 1.f;
+        if (u == 0) {
+          m_used = m_new;
+        } else if (m_new > m_used + 8.0f) {
+          bump = true;
+          factor = ex2(m_used - m_new);
+          m_used = m_new;
+        }
+        const bool need_o = bump && l > 0.f;
+        if (bump) l *= factor;
+        const float msub = m_used == -INFINITY ? 0.f : m_used;
+        float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = half * 64 + 2 * i;
+            const float a = ex2(fmaf(s[c], c2, -msub));
+            const float b = ex2(fmaf(s[c + 1], c2, -msub));
+            rs0 += a;
+            rs1 += b;
+            pk[i] = pack2<kBf16>(a, b);
+          }
+          tmem_st32(tS + 64 + half * 32, pk);
+        }
+        l += rs0 + rs1;
+        // O rescale (rare: only when the running max grew by more than 2^8)
+        if (__any_sync(0xffffffffu, need_o)) {
+          const float f = need_o ? factor : 1.f;
+#pragma unroll 1
+          for (int k = 0; k < D / 32; ++k) {
+            uint32_t r[32];
+            tmem_ld32(tO + k * 32, r);
+            tmem_wait_ld();
+            tmem_regs_ready(r);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+            tmem_st32(tO + k * 32, r);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[h]);
+      }
+      if (!ok) break;
+      // epilogue: O / l, LSE
+      float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float lse_v = l > 0.f ? (m_used + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+      char* orow = nullptr;
+      if (valid) {
+        const int orw = P.o_row_map ? __ldg(P.o_row_map + row) : row;
+        if ((unsigned)orw < (unsigned)P.N) {
+          orow = static_cast<char*>(P.o) +
+                 ((long long)bh * P.o_bh_stride + (long long)orw * P.o_row_stride) * 2;
+          if (P.lse) P.lse[(long long)bh * P.lse_bh_stride + orw] = lse_v;
+        }
+      }
+      const bool store = orow != nullptr;
+      if (nsup > 0) {
+        ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
+        ++to;
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 32; ++k) {
+          uint32_t r[32];
+          tmem_ld32(tO + k * 32, r);
+          tmem_wait_ld();
+          tmem_regs_ready(r);
+          if (store) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + k * 64);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack2<kBf16>(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+              w.y = pack2<kBf16>(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+              w.z = pack2<kBf16>(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+              w.w = pack2<kBf16>(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+              dst[v] = w;
+            }
+          }
+        }
+        tc_fence_before();
+      } else if (store) {
+        uint4* dst = reinterpret_cast<uint4*>(orow);
+        for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ------------------------------------------------------------- host side
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn get_encode() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+// [BH][N][D] 16-bit tensor, box = 64 columns x `rows` rows x 1 head, 128-byte swizzle.
+int make_tmap(CUtensorMap* m, const void* base, int dtype, int BH, int N, int D,
+              long long row_stride, long long bh_stride, int rows, const char* name) {
+  EncodeFn enc = get_encode();
+  if (!enc) return fail(PA_ERR_CUDA, "pa_attn_fwd: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)BH};
+  const cuuint64_t strides[2] = {(cuuint64_t)row_stride * 2, (cuuint64_t)bh_stride * 2};
+  const cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, dtype == PA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PA_ERR_ARG, "pa_attn_fwd: tensor map for %s rejected (CUresult %d): check "
+                "16-byte alignment of the base and strides", name, (int)r);
+  return PA_OK;
+}
+
+int check_args(const pa_attn_args* a, const char* who) {
+  PA_CHECK_ARG(a != nullptr, "%s: null args", who);
+  PA_CHECK_ARG(a->q && a->k && a->v && a->o, "%s: null q/k/v/o", who);
+  PA_CHECK_ARG(a->kv_num, "%s: null kv_num", who);
+  PA_CHECK_ARG(a->kv_stride >= 0, "%s: kv_stride=%d < 0", who, a->kv_stride);
+  PA_CHECK_ARG(a->kv_stride == 0 || (a->kv_idx && a->kv_partial),
+               "%s: null kv_idx / kv_partial", who);
+  PA_CHECK_ARG(a->BH >= 1 && a->N >= 1 && a->N < (1 << 24), "%s: bad BH=%d N=%d", who, a->BH,
+               a->N);
+  PA_CHECK_ARG(a->D == 64 || a->D == 128, "%s: D=%d unsupported (64 or 128)", who, a->D);
+  PA_CHECK_ARG(a->dtype == PA_BF16 || a->dtype == PA_F16, "%s: bad dtype %d", who, a->dtype);
+  PA_CHECK_ARG(a->BQ >= 1 && a->A >= 1, "%s: BQ=%d, A=%d must be positive", who, a->BQ, a->A);
+  PA_CHECK_ARG(a->N % a->BQ == 0 && a->N % a->A == 0,
+               "%s: N=%d must be a multiple of BQ=%d and A=%d", who, a->N, a->BQ, a->A);
+  PA_CHECK_ARG(a->A % 16 == 0 && (a->A <= 128 ? 128 % a->A == 0 : a->A % 128 == 0),
+               "%s: A=%d unsupported (16, 32, 64, 128 or a multiple of 128)", who, a->A);
+  PA_CHECK_ARG(a->N / a->A <= 65536 / 4, "%s: N/A=%d too many tiles per row", who,
+               a->N / a->A);
+  return PA_OK;
+}
+
+int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
+  CUtensorMap tq, tk, tv;
+  const int L = a->A < BN ? a->A : BN;
+  int rc;
+  if ((rc = make_tmap(&tq, a->q, a->dtype, a->BH, a->N, a->D, a->q_row_stride, a->q_bh_stride,
+                      BM, "q")))
+    return rc;
+  if ((rc = make_tmap(&tk, a->k, a->dtype, a->BH, a->N, a->D, a->k_row_stride, a->k_bh_stride,
+                      L, "k")))
+    return rc;
+  if ((rc = make_tmap(&tv, a->v, a->dtype, a->BH, a->N, a->D, a->v_row_stride, a->v_bh_stride,
+                      L, "v")))
+    return rc;
+  Pred pred;
+  if ((rc = make_pred(&a->pred, &pred, "pa_attn_fwd"))) return rc;
+  PA_CHECK_ARG(aligned(a->o, 16) && a->o_row_stride % 8 == 0 && a->o_bh_stride % 8 == 0,
+               "pa_attn_fwd: o must be 16-byte aligned with strides multiple of 8 elements");
+  FwdParams P;
+  P.BH = a->BH;
+  P.N = a->N;
+  P.A = a->A;
+  P.perm_q = a->perm_q;
+  P.perm_kv = a->perm_kv;
+  P.o_row_map = a->o_row_map;
+  P.o = a->o;
+  P.lse = a->lse;
+  P.o_bh_stride = a->o_bh_stride;
+  P.o_row_stride = a->o_row_stride;
+  P.lse_bh_stride = a->lse_bh_stride;
+  P.pred = pred;
+  const float scale = a->scale > 0.f ? a->scale : 1.0f / sqrtf((float)a->D);
+  P.scale_log2 = scale * 1.4426950408889634f;
+  P.pv = pv;
+  const uint32_t fmt = a->dtype == PA_BF16 ? 1u : 0u;
+  P.idesc_qk = make_idesc_f16(fmt, BM, BN, 0, 0);
+  P.idesc_pv = make_idesc_f16(fmt, BM, a->D, 0, 1);
+  P.total_items = pv.npairs * a->BH;
+
+  int dev = 0, sms = 148;
+  PA_CUDA(cudaGetDevice(&dev), "pa_attn_fwd");
+  PA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "pa_attn_fwd");
+  const int grid = P.total_items < sms ? P.total_items : sms;
+
+#define PA_LAUNCH(D_, L_, BF_)                                                              \
+  do {                                                                                      \
+    auto k = attn_fwd_kernel<D_, L_, BF_>;                                                  \
+    const int smem = Smem<D_>::kAlloc;                                                      \
+    PA_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),     \
+            "pa_attn_fwd");                                                                 \
+    k<<<grid, kThreads, smem, stream>>>(tq, tk, tv, P);                                     \
+  } while (0)
+#define PA_LAUNCH_L(D_, BF_)                       \
+  switch (L) {                                     \
+    case 16: PA_LAUNCH(D_, 16, BF_); break;        \
+    case 32: PA_LAUNCH(D_, 32, BF_); break;        \
+    case 64: PA_LAUNCH(D_, 64, BF_); break;        \
+    default: PA_LAUNCH(D_, 128, BF_); break;       \
+  }
+  if (a->D == 128) {
+    if (a->dtype == PA_BF16) { PA_LAUNCH_L(128, true) } else { PA_LAUNCH_L(128, false) }
+  } else {
+    if (a->dtype == PA_BF16) { PA_LAUNCH_L(64, true) } else { PA_LAUNCH_L(64, false) }
+  }
+#undef PA_LAUNCH_L
+#undef PA_LAUNCH
+  return check_launch("pa_attn_fwd");
+}
+
+}  // namespace
+}  // namespace pa
+
+extern "C" size_t pa_attn_workspace_size(const pa_attn_args* a) {
+  if (!a || a->N < 1 || a->A < 1) return 0;
+  return pa::plan_sizes(a->N, a->A).total;
+}
+
+extern "C" int pa_attn_plan(const pa_attn_args* a, void* ws, size_t ws_bytes,
+                            pa_stream_t stream) {
+  using namespace pa;
+  int rc = check_args(a, "pa_attn_plan");
+  if (rc) return rc;
+  const PlanSizes sz = plan_sizes(a->N, a->A);
+  PA_CHECK_ARG(ws && ws_bytes >= sz.total && aligned(ws, 256),
+               "pa_attn_plan: workspace must be 256-byte aligned and >= %zu bytes", sz.total);
+  const PlanView pv = plan_view(ws, a->N, a->A);
+  const size_t smem = 4ull * pv.cap;
+  if (smem > 48 * 1024)
+    PA_CUDA(cudaFuncSetAttribute(plan_pairs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem), "pa_attn_plan");
+  const cudaStream_t s = (cudaStream_t)stream;
+  plan_pairs_kernel<<<pv.npairs, kPlanThreads, smem, s>>>(a->kv_idx, a->kv_num, a->kv_partial,
+                                                         a->kv_stride, a->N, a->BQ, pv);
+  if ((rc = check_launch("pa_attn_plan"))) return rc;
+  plan_order_kernel<<<1, 256, 0, s>>>(pv);
+  return check_launch("pa_attn_plan");
+}
+
+extern "C" int pa_attn_fwd(const pa_attn_args* a, void* ws, size_t ws_bytes,
+                           pa_stream_t stream) {
+  using namespace pa;
+  int rc = check_args(a, "pa_attn_fwd");
+  if (rc) return rc;
+  const PlanSizes sz = plan_sizes(a->N, a->A);
+  PA_CHECK_ARG(ws && ws_bytes >= sz.total && aligned(ws, 256),
+               "pa_attn_fwd: workspace must be 256-byte aligned and >= %zu bytes", sz.total);
+  return launch_fwd(a, plan_view(ws, a->N, a->A), (cudaStream_t)stream);
+}
+
+extern "C" int pa_attn_status(const void* ws, int32_t* status_host, pa_stream_t stream) {
+  PA_CHECK_ARG(ws && status_host, "pa_attn_status: null pointer");
+  PA_CUDA(cudaMemcpyAsync(status_host, ws, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                          (cudaStream_t)stream), "pa_attn_status");
+  PA_CUDA(cudaStreamSynchronize((cudaStream_t)stream), "pa_attn_status");
+  return *status_host ? PA_ERR_DEVICE : PA_OK;
+}

@@ -1,0 +1,93 @@
+"""Attention over a union of differing mask families by disjoint split + LSE merge.
+
+A mask M that is the disjoint union of parts P1 + P2 + ... is computed as one
+block-sparse attention per part -- each part in its own best basis (identity or a
+class A residue permutation) -- and the partial (O_i, LSE_i) are combined with the
+log-sum-exp merge.  This is the execution side of the reference's composition
+study (src/polyattn/experiments/compose.py:7-17: split, per-part class-A basis,
+merge), which the reference only counts.  Disjointness is required: an element in
+two parts would be counted twice in the softmax denominator.
+
+The permuted part gathers Q/K/V once into residue order, evaluates the predicate in
+original coordinates (perm_q = perm_kv = perm) and writes its O/LSE rows straight
+back to original order (o_row_map = perm), so the merge needs no row map.
+"""
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import attention, blockindex, masks, merge, permute
+
+
+@dataclass
+class SplitPart:
+    mask: object            # polyhedral_b200.masks object (has .spec)
+    BQ: int
+    A: int
+    stride: int = 0         # residue-permutation stride; 0 = identity basis
+
+
+class SplitPlan:
+    """Mask-only preprocessing of a split (block indices, permutations, work
+    lists), built once and reused by ``run`` for every (q, k, v)."""
+
+    def __init__(self, parts, N, device="cuda"):
+        self.N = N
+        self.parts = list(parts)
+        self.device = torch.device(device)
+        self.perms, self.indices, self.plans = [], [], []
+        for part in self.parts:
+            perm = None
+            if part.stride:
+                perm = permute.residue_perm_device(N, part.stride, self.device)
+            dbi = blockindex.build_device(part.mask, N, part.BQ, part.A, perm_q=perm,
+                                          perm_kv=perm, device=self.device)
+            plan = attention.make_plan(dbi.kv_idx, dbi.kv_num, dbi.kv_partial, N, part.BQ,
+                                       part.A)
+            self.perms.append(perm)
+            self.indices.append(dbi)
+            self.plans.append(plan)
+
+    def run(self, q, k, v, scale=None, out=None):
+        """(o, lse) of the union mask, rows in original order."""
+        o = lse = None
+        for i, part in enumerate(self.parts):
+            kind, p0, p1, p2 = part.mask.spec
+            perm = self.perms[i]
+            if perm is None:
+                qi, ki, vi = q, k, v
+            else:
+                qi, ki, vi = permute.apply_perm_many((q, k, v), perm)
+            oi, li = attention.block_sparse_attention(
+                qi, ki, vi, None, None, None, kind, p0, p1, p2, part.BQ, part.A,
+                scale=scale, perm_q=perm, perm_kv=perm, o_row_map=perm,
+                plan=self.plans[i], return_lse=True,
+                out=(out if (i == 0 and out is not None) else None))
+            if o is None:
+                o, lse = oi, li
+            else:
+                o, lse = merge.lse_merge(o, lse, oi, li, out=o, lse_out=lse)
+        return o, lse
+
+    def live_count(self):
+        return sum(int(p.mask.live_count(self.N)) for p in self.parts)
+
+
+def local_strided_split(w, s, N, BQ=128, A=32, stride=None, device="cuda"):
+    """LocalStrided(w, s) = SlidingWindow(w) [identity] + FarStrided(w, s)
+    [residue permutation by `stride`, default s]."""
+    parts = [SplitPart(masks.SlidingWindow(w), BQ, A, 0),
+             SplitPart(masks.FarStrided(w, s), BQ, A, stride or s)]
+    return SplitPlan(parts, N, device)
+
+
+def check_disjoint_cover(union_mask, parts, N):
+    """True when the parts are pairwise disjoint and their union is the mask
+    (compose.py:69-70 asserts exact reconstruction).  Host check, small N."""
+    M = union_mask.dense(N)
+    acc = np.zeros_like(M, dtype=np.int32)
+    for p in parts:
+        acc += p.mask.dense(N).astype(np.int32)
+    return bool((acc <= 1).all() and np.array_equal(acc.astype(bool), M))
