@@ -234,7 +234,7 @@ def run_ours(args, rank, world, device):
         torch.cuda.synchronize(device)
         t_ms = ev0.elapsed_time(ev1)
         # keep the same load running (untimed) so the sampler sees >= 1 s of it
-        extra = int(max(0.0, 1000.0 - t_ms) / max(t_ms / args.steps, 1e-3))
+        extra = 0 if args.profile else int(max(0.0, 1000.0 - t_ms) / max(t_ms / args.steps, 1e-3))
         for i in range(extra):
             do_step(i)
         torch.cuda.synchronize(device)
@@ -267,7 +267,7 @@ def run_ours(args, rank, world, device):
 
     # end to end through the public API with host buffers (rank-local)
     e2e = None
-    if rank == 0 or world > 1:
+    if not args.profile:
         hq = [x.cpu().pin_memory() for x in bufs[0]]
         ho = torch.empty(B * H, N, D, dtype=torch.bfloat16).pin_memory()
         hl = torch.empty(B * H, N, dtype=torch.float32).pin_memory()
@@ -308,7 +308,7 @@ def run_ours(args, rank, world, device):
                 "peak_source": f"{peak_kind} bf16 dense (burst)"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not (args.no_cpu or args.profile):
         cpu = cpu_baseline(wl, budget_s=args.cpu_budget)
 
     if rank == 0:
@@ -423,6 +423,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="short run for ncu: no clock fill, no end-to-end leg, no CPU leg")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
