@@ -76,12 +76,15 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, enabled=True):
         self.gpu = gpu_index
+        self.enabled = enabled
         self.proc = None
         self.lines = []
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -122,6 +125,25 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def max_over_ranks(x, device=None):
+    """Max of a float over all ranks of the default process group (identity when
+    there is none); CUDA tensor under NCCL, CPU tensor under gloo."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(x)
+    dev = device if dist.get_backend() == "nccl" else torch.device("cpu")
+    t = torch.tensor([float(x)], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def aggregate_tflops(flops_per_rank, world, ms_per_step):
+    """Whole-job throughput: every rank does `flops_per_rank` per step and the job's
+    step time is the slowest rank's."""
+    return flops_per_rank * world / (ms_per_step * 1e-3) / 1e12
 
 
 def live_flops(B, H, N, D, name):
@@ -225,7 +247,8 @@ def run_ours(args, rank, world, device):
     if st:
         raise RuntimeError(f"attention kernel reported device status {st} during warm-up")
 
-    with ClockSampler(device.index if device.index is not None else 0) as clk:
+    with ClockSampler(device.index if device.index is not None else 0,
+                      enabled=not args.profile) as clk:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
         for i in range(args.steps):
@@ -238,13 +261,11 @@ def run_ours(args, rank, world, device):
         for i in range(extra):
             do_step(i)
         torch.cuda.synchronize(device)
+    t_ms = max_over_ranks(t_ms, device)
     if world > 1:
-        t = torch.tensor([t_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_ms = float(t.item())
         dist.barrier()
     ms_per_step = t_ms / args.steps
-    value = flops * world / (ms_per_step * 1e-3) / 1e12
+    value = aggregate_tflops(flops, world, ms_per_step)
 
     # dominant kernel alone, CUDA events on the launching stream
     kernel_ms = None
@@ -287,12 +308,8 @@ def run_ours(args, rank, world, device):
             hl.copy_(lse, non_blocking=True)
         e1.record()
         torch.cuda.synchronize(device)
-        e2e_ms = e0.elapsed_time(e1) / e2e_steps
-        if world > 1:
-            t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
-        e2e = {"value": round(flops * world / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, device)
+        e2e = {"value": round(aggregate_tflops(flops, world, e2e_ms), 3), "unit": "TFLOP/s",
                "ms_per_step": round(e2e_ms, 4),
                "h2d_bytes_per_step": 3 * B * H * N * D * 2,
                "d2h_bytes_per_step": B * H * N * D * 2 + B * H * N * 4}
