@@ -174,6 +174,19 @@ PA_API int pa_attn_fwd(const pa_attn_args* args, void* workspace, size_t workspa
  * workspace until the next plan. */
 PA_API int pa_attn_status(const void* workspace, int32_t* status_host, pa_stream_t stream);
 
+/* pa_attn_plan + pa_attn_fwd without a caller workspace.  No counterpart in the
+ * reference: it exists for callers that may not allocate device memory (a host
+ * embedding that only hands over tensors it already owns, a process working
+ * inside a fixed memory budget or another framework's pool).  The work list goes
+ * to a 4 MiB array compiled into the library, which every GPU that loads the
+ * library holds until exit; a request whose work list would not fit (see
+ * pa_attn_workspace_size; about N <= 57344 at A = 16) is rejected with PA_ERR_ARG.
+ * The first call on a device looks up that array's device address (do it before
+ * any stream capture).  All calls share the array and each rebuilds what it
+ * reads; calls that overlap on the GPU race on it and must be ordered by the
+ * caller.  Allocates nothing. */
+PA_API int pa_attn_fwd_noalloc(const pa_attn_args* args, pa_stream_t stream);
+
 /* ------------------------------------------------------------ LSE merge
  * Attention over a disjoint union M = P1 + P2 from the attentions over P1 and P2
  * (src/polyattn/experiments/compose.py:7-17): per row, m = max(l1, l2),

@@ -68,6 +68,7 @@ SIGNATURES = {
     "pa_attn_plan": (ctypes.c_int, [ctypes.POINTER(PaAttnArgs), c_vp, c_sz, c_vp]),
     "pa_attn_fwd": (ctypes.c_int, [ctypes.POINTER(PaAttnArgs), c_vp, c_sz, c_vp]),
     "pa_attn_status": (ctypes.c_int, [c_vp, ctypes.POINTER(c_i32), c_vp]),
+    "pa_attn_fwd_noalloc": (ctypes.c_int, [ctypes.POINTER(PaAttnArgs), c_vp]),
     "pa_lse_merge": (ctypes.c_int, [ctypes.POINTER(PaMergeArgs), c_vp]),
 }
 

@@ -21,7 +21,8 @@ INCLUDE = ROOT / "include"
 BUILD = PKG / "_build"
 LIB = PKG / "libpolyattn_sm100.so"
 
-SOURCES = ["capi_util.cu", "blockindex.cu", "permute.cu", "merge.cu", "attn.cu"]
+SOURCES = ["capi_util.cu", "blockindex.cu", "permute.cu", "merge.cu", "attn.cu",
+           "attn_noalloc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
