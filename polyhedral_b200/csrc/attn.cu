@@ -49,6 +49,7 @@ constexpr uint32_t kDrainLimitNs = 200u * 1000u * 1000u;
 // ----------------------------------------------------------------- plan layout
 struct PlanView {
   int32_t* err;        // status word
+  int32_t* sched;      // [2]: next work item, CTAs finished (reset by the last CTA)
   int32_t* pair_cnt;   // [npairs] union entries of pair p
   int32_t* order;      // [npairs] pairs sorted by decreasing entry count
   int32_t* entries;    // [npairs * cap] ascending A-tile ids
@@ -79,7 +80,8 @@ PlanSizes plan_sizes(int N, int A) {
 PlanView plan_view(void* ws, int N, int A) {
   const PlanSizes s = plan_sizes(N, A);
   char* b = static_cast<char*>(ws);
-  return PlanView{reinterpret_cast<int32_t*>(b), reinterpret_cast<int32_t*>(b + s.off_cnt),
+  return PlanView{reinterpret_cast<int32_t*>(b), reinterpret_cast<int32_t*>(b + 64),
+                  reinterpret_cast<int32_t*>(b + s.off_cnt),
                   reinterpret_cast<int32_t*>(b + s.off_order),
                   reinterpret_cast<int32_t*>(b + s.off_entries),
                   reinterpret_cast<uint8_t*>(b + s.off_status), s.cap, s.npairs};
@@ -170,7 +172,8 @@ plan_pairs_kernel(const int32_t* __restrict__ kv_idx, const int32_t* __restrict_
   if (threadIdx.x == 0) pv.pair_cnt[p] = total;
 }
 
-// Longest-first order of the pairs (stable on ties), for the static schedule.
+// Longest-first order of the pairs (stable on ties); work item `it` of the forward
+// is pair order[it / BH] of head it % BH, fetched dynamically by the CTAs.
 __global__ void plan_order_kernel(PlanView pv) {
   const int n = pv.npairs;
   for (int p = threadIdx.x; p < n; p += blockDim.x) {
@@ -182,7 +185,11 @@ __global__ void plan_order_kernel(PlanView pv) {
     }
     pv.order[rank] = p;
   }
-  if (threadIdx.x == 0) *pv.err = 0;   // a new plan starts with a clean status
+  if (threadIdx.x == 0) {
+    *pv.err = 0;   // a new plan starts with a clean status
+    pv.sched[0] = 0;
+    pv.sched[1] = 0;
+  }
 }
 
 // ------------------------------------------------------------- forward kernel
@@ -208,9 +215,10 @@ struct Smem {
   static constexpr int kQOff = 0;
   static constexpr int kKVOff = 2 * kTileBytes;
   static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
-  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] drain kv_full[S] kv_empty[S]
-  static constexpr int kNumBars = 11 + 2 * kSlots;
-  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort flag
+  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] drain item_full[2]
+  //           item_empty[2] kv_full[S] kv_empty[S]
+  static constexpr int kNumBars = 15 + 2 * kSlots;
+  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
   static constexpr int kColOff = (kMiscOff + 16 + 15) & ~15;  // per-warp column coords [8][128]
   static constexpr int kBytes = kColOff + 8 * 128 * 4;
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
@@ -261,45 +269,110 @@ __device__ __forceinline__ SegInfo seg_info(const FwdParams& P, const int32_t* e
   return SegInfo{__ldg(ent + e) * P.A + (u - e * sub) * BN, (int)__ldg(sts + e)};
 }
 
-// Live bits of columns [32k, 32k + 32) of super-tile row `irow` (original row
-// index): bit c set when column 32k + c is live.  Dead segments give 0, full
-// segments all ones, partial segments evaluate the predicate per element
-// (`cols` holds original column indices when K/V rows are permuted).
-template <int L>
-__device__ __forceinline__ uint32_t chunk_mask(const Pred& pred, int k, const SegInfo* si,
-                                               int irow, const int* cols) {
-  if constexpr (L >= 32) {
-    constexpr int per = L / 32;
-    const SegInfo g = si[k / per];
-    if (g.st == 0) return 0u;
-    if (g.st == 1) return 0xffffffffu;
-    const int cbase = (k % per) * 32;
-    uint32_t w = 0;
-#pragma unroll 1
-    for (int c = 0; c < 32; ++c) {
-      const int j = cols ? cols[k * 32 + c] : g.row0 + cbase + c;
-      w |= (uint32_t)pred_live(pred, irow, j) << c;
-    }
-    return w;
-  } else {
-    uint32_t w = 0;
-#pragma unroll
-    for (int hw = 0; hw < 2; ++hw) {
-      const SegInfo g = si[2 * k + hw];
-      uint32_t b = 0;
-      if (g.st == 1) {
-        b = 0xffffu;
-      } else if (g.st == 2) {
-#pragma unroll 1
-        for (int c = 0; c < 16; ++c) {
-          const int j = cols ? cols[k * 32 + hw * 16 + c] : g.row0 + c;
-          b |= (uint32_t)pred_live(pred, irow, j) << c;
-        }
-      }
-      w |= b << (16 * hw);
-    }
-    return w;
+// floor(a / b) for b > 0
+__device__ __forceinline__ int floordiv(int a, int b) {
+  return a >= 0 ? a / b : -((-a + b - 1) / b);
+}
+
+// Bits (c - base) for c in [lo, hi], clipped to the word [base, base + 32).
+__device__ __forceinline__ uint32_t range_bits(int lo, int hi, int base) {
+  lo = max(lo - base, 0);
+  hi = min(hi - base, 31);
+  if (hi < lo) return 0u;
+  const uint32_t upto = hi == 31 ? 0xffffffffu : ((2u << hi) - 1u);
+  return upto & ~((1u << lo) - 1u);
+}
+
+// Live bits of columns [base, base + 32) of a segment of `len` columns whose
+// original indices form the progression j0 + c*dj (dj >= 1), for the row with
+// original index i = j0 + e.  With d = e - c*dj decreasing in c, every kind is a
+// union of at most two ranges of c, and a lattice term (d % m == 0) is constant
+// over the segment when m divides dj.  Returns false when it is not (the caller
+// then evaluates element by element).
+__device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, int dj, int base,
+                                                 int len, uint32_t& out) {
+  const int cz = floordiv(e, dj);                       // d >= 0  <=>  c <= cz
+  int lo1 = 0, hi1 = -1, lo2 = 0, hi2 = -1;
+  bool lattice = false;
+  if (p.mod > 0) {
+    if (dj % p.mod) return false;
+    lattice = (((e % p.mod) + p.mod) % p.mod) == 0;
   }
+  switch (p.kind) {
+    case PA_CAUSAL:
+      hi1 = cz;
+      break;
+    case PA_WINDOW:                                     // d < p0 <=> c > (e - p0) / dj
+      lo1 = floordiv(e - p.p0, dj) + 1;
+      hi1 = cz;
+      break;
+    case PA_DILATED:
+      hi1 = lattice ? cz : -1;
+      break;
+    case PA_LOCAL_STRIDED:
+      lo1 = floordiv(e - p.p0, dj) + 1;
+      hi1 = cz;
+      hi2 = lattice ? cz : -1;
+      break;
+    case PA_TWOBAND:
+      lo1 = floordiv(e - p.p0, dj) + 1;
+      hi1 = cz;
+      lo2 = floordiv(e - p.p1 - p.p2, dj) + 1;
+      hi2 = min(cz, floordiv(e - p.p1, dj));
+      break;
+    case PA_SINKS:                                      // kv < p1 <=> c <= (p1 - j0 - 1) / dj
+      lo1 = floordiv(e - p.p0, dj) + 1;
+      hi1 = cz;
+      hi2 = min(cz, floordiv(p.p1 - j0 - 1, dj));
+      break;
+    case PA_FAR_STRIDED:                                // d >= p0 <=> c <= (e - p0) / dj
+      hi1 = lattice ? min(cz, floordiv(e - p.p0, dj)) : -1;
+      break;
+    default:
+      return false;
+  }
+  hi1 = min(hi1, len - 1);
+  hi2 = min(hi2, len - 1);
+  out = range_bits(lo1, hi1, base) | range_bits(lo2, hi2, base);
+  return true;
+}
+
+// Live bits of `n` (<= 32) columns evaluated one by one; column c has original
+// index cols[c] when given, else j0 + (base + c) * dj.
+__device__ __forceinline__ uint32_t element_bits(const Pred& p, int i, const int* cols, int j0,
+                                                 int dj, int base, int n) {
+  uint32_t w = 0;
+#pragma unroll 1
+  for (int c = 0; c < n; ++c) {
+    const int j = cols ? cols[c] : j0 + (base + c) * dj;
+    w |= (uint32_t)pred_live(p, i, j) << c;
+  }
+  return w;
+}
+
+// d = a * b + c on two lanes at once (f32x2).
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+// a += b on two lanes at once (f32x2).
+__device__ __forceinline__ void fadd2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb;\n\t"
+      "mov.b64 ra, {%0, %1};\n\t"
+      "mov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 ra, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <int D, int L, bool kBf16>
@@ -323,10 +396,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint64_t* p_full = bars + 6;
   uint64_t* o_full = bars + 8;
   uint64_t* drain = bars + 10;
-  uint64_t* kv_full = bars + 11;
-  uint64_t* kv_empty = bars + 11 + NS;
+  uint64_t* item_full = bars + 11;
+  uint64_t* item_empty = bars + 13;
+  uint64_t* kv_full = bars + 15;
+  uint64_t* kv_empty = bars + 15 + NS;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
+  volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
   int* colbuf = reinterpret_cast<int*>(smem + SM::kColOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -341,6 +417,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       mbar_init(&o_full[h], 1);
     }
     mbar_init(drain, 1);
+    for (int r = 0; r < 2; ++r) {
+      mbar_init(&item_full[r], 1);
+      mbar_init(&item_empty[r], 1 + 8);   // MMA thread + one lane per softmax warp
+    }
     for (int s = 0; s < NS; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -362,7 +442,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  const int npairs = P.pv.npairs;
 
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ producer
@@ -370,9 +449,21 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       int qi = 0;
       int q_armed[2] = {0, 0};
       uint32_t kv_g = 0;
-      for (int it = blockIdx.x; it < P.total_items && !*s_abort; it += gridDim.x) {
-        const int bh = it / npairs;
-        const int p = __ldg(P.pv.order + (it - bh * npairs));
+      uint32_t ring = 0;
+      while (true) {
+        // fetch the next work item and hand it to the MMA and softmax warps
+        int it = atomicAdd(P.pv.sched, 1);
+        if (it >= P.total_items || *s_abort) it = -1;
+        const uint32_t rs = ring & 1;
+        if (ring >= 2 &&
+            !mbar_wait(&item_empty[rs], ((ring >> 1) - 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM))
+          break;
+        s_item[rs] = it;
+        mbar_arrive(&item_full[rs]);
+        ++ring;
+        if (it < 0) break;
+        const int p = __ldg(P.pv.order + it / P.BH);
+        const int bh = it - (it / P.BH) * P.BH;
         const int cnt = __ldg(P.pv.pair_cnt + p);
         const int nsup = num_super<L>(P, cnt);
         if (nsup == 0) continue;
@@ -470,9 +561,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         tc_fence_after();
         return r;
       };
-      for (int it = blockIdx.x; it < P.total_items && ok; it += gridDim.x) {
-        const int bh = it / npairs;
-        const int p = __ldg(P.pv.order + (it - bh * npairs));
+      uint32_t ring = 0;
+      while (ok) {
+        const uint32_t rs = ring & 1;
+        if (!(ok = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM)))
+          break;
+        const int it = s_item[rs];
+        mbar_arrive(&item_empty[rs]);
+        ++ring;
+        if (it < 0) break;
+        const int p = __ldg(P.pv.order + it / P.BH);
         const int nsup = num_super<L>(P, __ldg(P.pv.pair_cnt + p));
         if (nsup == 0) continue;
         ok = mbar_wait(&q_full[0], qi & 1, s_abort, err, DEV_TIMEOUT_Q) &&
@@ -528,9 +626,18 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     int* mycols = colbuf + warp * 128;
     uint32_t ts = 0, to = 0;
     const float c2 = P.scale_log2;
-    for (int it = blockIdx.x; it < P.total_items; it += gridDim.x) {
-      const int bh = it / npairs;
-      const int p = __ldg(P.pv.order + (it - bh * npairs));
+    uint32_t ring = 0;
+    while (true) {
+      const uint32_t rs = ring & 1;
+      bool got = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM);
+      if (!__all_sync(0xffffffffu, got)) break;
+      const int it = s_item[rs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[rs]);
+      ++ring;
+      if (it < 0) break;
+      const int p = __ldg(P.pv.order + it / P.BH);
+      const int bh = it - (it / P.BH) * P.BH;
       const int cnt = __ldg(P.pv.pair_cnt + p);
       const int nsup = num_super<L>(P, cnt);
       const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
@@ -541,34 +648,87 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       float m_used = -INFINITY, l = 0.f;
       bool ok = true;
       for (int u = 0; u < nsup; ++u) {
+        // segments of this super-tile, as seen by this half; for partial ones the
+        // original column indices, as a progression j0 + c*dj when they form one
         SegInfo si[S];
-        int any_partial = 0;
+        int j0s[S], djs[S];
+        bool aps[S];
 #pragma unroll
         for (int sg = 0; sg < S; ++sg) {
           si[sg] = seg_info<L>(P, ent, sts, cnt, u, sg);
           si[sg].st = (si[sg].st >> (2 * h)) & 3;
-          any_partial |= si[sg].st == 2;
+          j0s[sg] = si[sg].row0;
+          djs[sg] = 1;
+          aps[sg] = true;
         }
-        if (any_partial && P.perm_kv) {
-          __syncwarp();
+        if (P.perm_kv) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int c = k * 32 + lane;
-            const int sg = c / L;
-            int j = -1;
+          for (int sg = 0; sg < S; ++sg) {
+            if (si[sg].st != 2) continue;                 // uniform across the warp
+            constexpr int PER = (L + 31) / 32;
+            int v[PER];
+            bool okp = true;
 #pragma unroll
-            for (int q = 0; q < S; ++q)
-              if (q == sg && si[q].st == 2) j = __ldg(P.perm_kv + si[q].row0 + (c - q * L));
-            mycols[c] = j;
+            for (int t = 0; t < PER; ++t) {
+              const int c = t * 32 + lane;
+              v[t] = c < L ? __ldg(P.perm_kv + si[sg].row0 + c) : 0;
+            }
+            const int j0 = __shfl_sync(0xffffffffu, v[0], 0);
+            const int dj = __shfl_sync(0xffffffffu, v[0], 1) - j0;
+#pragma unroll
+            for (int t = 0; t < PER; ++t) {
+              const int c = t * 32 + lane;
+              if (c < L) okp &= v[t] == j0 + c * dj;
+            }
+            okp = __all_sync(0xffffffffu, okp && dj >= 1);
+            j0s[sg] = j0;
+            djs[sg] = dj;
+            aps[sg] = okp;
+            if (!okp) {
+              __syncwarp();
+#pragma unroll
+              for (int t = 0; t < PER; ++t) {
+                const int c = t * 32 + lane;
+                if (c < L) mycols[sg * L + c] = v[t];
+              }
+              __syncwarp();
+            }
           }
-          __syncwarp();
         }
         // live bits of this row for the 128 columns, computed while S is in flight
         uint32_t mk[4];
-        {
-          const int* cols = (any_partial && P.perm_kv) ? mycols : nullptr;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) mk[k] = chunk_mask<L>(P.pred, k, si, irow, cols);
+        for (int k = 0; k < 4; ++k) {
+          if constexpr (L >= 32) {
+            constexpr int per = L / 32;
+            const int sg = k / per, base = (k % per) * 32;
+            const int st = si[sg].st;
+            uint32_t w = st == 1 ? 0xffffffffu : 0u;
+            if (st == 2) {
+              if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg], base,
+                                                L, w)))
+                w = element_bits(P.pred, irow, aps[sg] ? nullptr : mycols + sg * L + base,
+                                 j0s[sg], djs[sg], base, 32);
+            }
+            mk[k] = w;
+          } else {
+            uint32_t w = 0;
+#pragma unroll
+            for (int hw = 0; hw < 2; ++hw) {
+              const int sg = 2 * k + hw;
+              const int st = si[sg].st;
+              uint32_t b = st == 1 ? 0xffffu : 0u;
+              if (st == 2) {
+                if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg], 0,
+                                                  L, b)))
+                  b = element_bits(P.pred, irow, aps[sg] ? nullptr : mycols + sg * L, j0s[sg],
+                                   djs[sg], 0, 16);
+                b &= 0xffffu;
+              }
+              w |= b << (16 * hw);
+            }
+            mk[k] = w;
+          }
         }
         ok = mbar_wait(&s_full[h], ts & 1, s_abort, err, DEV_TIMEOUT_S);
         ++ts;
@@ -602,9 +762,18 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
               if (!((mk[k] >> i) & 1u)) s[k * 32 + i] = -INFINITY;
           }
         }
-        float mx = -INFINITY;
+        float mx;
+        {
+          float m8[8];
 #pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, s[c]);
+          for (int j = 0; j < 8; ++j) m8[j] = fmaxf(s[2 * j], s[2 * j + 1]);
+#pragma unroll
+          for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) m8[j] = fmax3(m8[j], s[c + 2 * j], s[c + 2 * j + 1]);
+          }
+          mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        }
         const float m_tile = mx * c2;
         const float m_new = fmaxf(m_used, m_tile);
         bool bump = false;
@@ -619,22 +788,26 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         const bool need_o = bump && l > 0.f;
         if (bump) l *= factor;
         const float msub = m_used == -INFINITY ? 0.f : m_used;
-        float rs0 = 0.f, rs1 = 0.f;
+        float r8[8];
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
+        for (int j = 0; j < 8; ++j) r8[j] = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = half * 64 + 2 * i;
-            const float a = ex2(fmaf(s[c], c2, -msub));
-            const float b = ex2(fmaf(s[c + 1], c2, -msub));
-            rs0 += a;
-            rs1 += b;
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int c = q4 * 32 + 2 * i;
+            float x0, x1;
+            ffma2(x0, x1, s[c], s[c + 1], c2, -msub);
+            const float a = ex2(x0);
+            const float b = ex2(x1);
+            const int j = (2 * i) & 7;
+            fadd2(r8[j], r8[j + 1], a, b);
             pk[i] = pack2<kBf16>(a, b);
           }
-          tmem_st32(tS + 64 + half * 32, pk);
+          tmem_st16(tS + 64 + q4 * 16, pk);
         }
-        l += rs0 + rs1;
+        l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
         // O rescale (rare: only when the running max grew by more than 2^8)
         if (__any_sync(0xffffffffu, need_o)) {
           const float f = need_o ? factor : 1.f;
@@ -705,6 +878,14 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+  if (threadIdx.x == 0) {
+    // the last CTA to finish rewinds the work counter for the next launch
+    __threadfence();
+    if (atomicAdd(P.pv.sched + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(P.pv.sched, 0);
+      atomicExch(P.pv.sched + 1, 0);
+    }
+  }
 }
 
 // ------------------------------------------------------------- host side

@@ -21,6 +21,7 @@ enum : int32_t {
   DEV_TIMEOUT_P = 4,        // MMA waited too long for P
   DEV_TIMEOUT_O = 5,        // epilogue waited too long for O
   DEV_TIMEOUT_DRAIN = 6,    // teardown could not drain outstanding copies
+  DEV_TIMEOUT_ITEM = 7,     // a wait on the work-item ring ran out
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer.  One kernel step
@@ -165,6 +166,15 @@ PA_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
         "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
         "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
         "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+PA_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0],"
+      " {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+        "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
+        "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 PA_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
