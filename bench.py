@@ -176,7 +176,8 @@ class Pipeline:
             self.perm = permute.residue_perm_device(N, s, device) if s else None
             dbi = blockindex.build_device(masks_gpu.numpy_mask(name), N, BQ, A,
                                           perm_q=self.perm, perm_kv=self.perm, device=device)
-            self.plan = attention.make_plan(dbi.kv_idx, dbi.kv_num, dbi.kv_partial, N, BQ, A)
+            self.plan = attention.make_plan(dbi.kv_idx, dbi.kv_num, dbi.kv_partial, N, BQ, A,
+                                            perm_kv=self.perm)
             self.dbi = dbi
         torch.cuda.synchronize(device)
         self.index_ms = (time.perf_counter() - t0) * 1e3

@@ -158,8 +158,9 @@ PA_API size_t pa_attn_workspace_size(const pa_attn_args* args);
 
 /* Builds, in `workspace`, the per-256-row work list the forward kernel runs on
  * (union of the listed tiles of the two 128-row halves, with each half's
- * full/partial/dead status, ordered longest first).  Depends only on the block
- * index: it can be built once and reused by every pa_attn_fwd on the same index. */
+ * full/partial/dead status and the original column indices of every listed tile,
+ * ordered longest first).  Depends only on the block index and perm_kv: it can be
+ * built once and reused by every pa_attn_fwd with the same index and perm_kv. */
 PA_API int pa_attn_plan(const pa_attn_args* args, void* workspace, size_t workspace_bytes,
                  pa_stream_t stream);
 
@@ -180,7 +181,8 @@ PA_API int pa_attn_status(const void* workspace, int32_t* status_host, pa_stream
  * inside a fixed memory budget or another framework's pool).  The work list goes
  * to a 4 MiB array compiled into the library, which every GPU that loads the
  * library holds until exit; a request whose work list would not fit (see
- * pa_attn_workspace_size; about N <= 57344 at A = 16) is rejected with PA_ERR_ARG.
+ * pa_attn_workspace_size; about N <= 36096 at A = 16, 51200 at A = 32) is rejected
+ * with PA_ERR_ARG.
  * The first call on a device looks up that array's device address (do it before
  * any stream capture).  All calls share the array and each rebuilds what it
  * reads; calls that overlap on the GPU race on it and must be ordered by the

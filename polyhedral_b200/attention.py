@@ -29,16 +29,20 @@ _DTYPES = {torch.bfloat16: _lib.PA_BF16, torch.float16: _lib.PA_F16}
 
 
 class AttnPlan:
-    """Device work list for one block index (``pa_attn_plan``): the per-256-row
-    union of listed tiles with each 128-row half's dead/full/partial status,
-    ordered longest first.  Reusable by every forward on the same index."""
+    """Device work list for one block index and K/V permutation (``pa_attn_plan``):
+    the per-256-row union of listed tiles with each 128-row half's
+    dead/full/partial status, the original-column progression of every listed
+    tile, ordered longest first.  Reusable by every forward on the same index and
+    ``perm_kv``."""
 
-    def __init__(self, kv_idx, kv_num, kv_partial, N, BQ, A, device=None):
+    def __init__(self, kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=None, device=None):
         device = device or kv_num.device
         self.N, self.BQ, self.A = int(N), int(BQ), int(A)
         self.kv_idx, self.kv_num, self.kv_partial = kv_idx, kv_num, kv_partial
         self.kv_stride = int(kv_idx.shape[1]) if kv_idx.dim() == 2 else 0
+        self.perm_kv = _perm(perm_kv, N, device)
         a = _args_skeleton(N, BQ, A, kv_idx, kv_num, kv_partial, self.kv_stride)
+        a.perm_kv = _ptr(self.perm_kv)
         nbytes = _lib.load().pa_attn_workspace_size(ctypes.byref(a))
         self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
         _lib.call("pa_attn_plan", ctypes.byref(a), self.workspace.data_ptr(), nbytes,
@@ -65,16 +69,18 @@ def _args_skeleton(N, BQ, A, kv_idx, kv_num, kv_partial, kv_stride):
     a.kv_num = _ptr(kv_num)
     a.kv_partial = _ptr(kv_partial) if kv_stride else None
     a.kv_stride = int(kv_stride)
-    # placeholders: the plan reads only the block index
+    # placeholders: the plan reads only the block index and perm_kv
     a.q = a.k = a.v = a.o = _ptr(kv_num)
     return a
 
 
-def make_plan(kv_idx, kv_num, kv_partial, N, BQ, A):
-    """Build the forward's work list once for a block index."""
+def make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=None):
+    """Build the forward's work list once for a block index (and the K/V
+    permutation the forward will be given, if any)."""
     return AttnPlan(_index_tensor(kv_idx, torch.int32, kv_num.device),
                     _index_tensor(kv_num, torch.int32, kv_num.device),
-                    _index_tensor(kv_partial, torch.int8, kv_num.device), N, BQ, A)
+                    _index_tensor(kv_partial, torch.int8, kv_num.device), N, BQ, A,
+                    perm_kv=perm_kv)
 
 
 def _index_tensor(t, dtype, device):
@@ -122,9 +128,14 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     rmap = _perm(o_row_map, N, dev)
 
     if plan is None:
-        plan = make_plan(kv_idx, kv_num, kv_partial, N, BQ, A)
-    elif (plan.N, plan.BQ, plan.A) != (N, BQ, A):
-        raise ValueError("plan was built for a different (N, BQ, A)")
+        plan = make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=pk)
+    else:
+        if (plan.N, plan.BQ, plan.A) != (N, BQ, A):
+            raise ValueError("plan was built for a different (N, BQ, A)")
+        if (plan.perm_kv is None) != (pk is None) or (
+                pk is not None and plan.perm_kv.data_ptr() != pk.data_ptr()
+                and not torch.equal(plan.perm_kv, pk)):
+            raise ValueError("plan was built for a different perm_kv")
 
     o = out if out is not None else torch.empty((BH, N, D), dtype=q.dtype, device=dev)
     lse = None

@@ -54,6 +54,7 @@ struct PlanView {
   int32_t* order;      // [npairs] pairs sorted by decreasing entry count
   int32_t* entries;    // [npairs * cap] ascending A-tile ids
   uint8_t* status;     // [npairs * cap] bits 0-1 half 0, bits 2-3 half 1: 0 dead 1 full 2 partial
+  uint2* desc;         // [npairs * cap] per listed tile: see make_desc below
   int cap;
   int npairs;
 };
@@ -61,7 +62,7 @@ struct PlanView {
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct PlanSizes {
-  size_t off_cnt, off_order, off_entries, off_status, total;
+  size_t off_cnt, off_order, off_entries, off_status, off_desc, total;
   int cap, npairs;
 };
 
@@ -73,7 +74,8 @@ PlanSizes plan_sizes(int N, int A) {
   s.off_order = align_up(s.off_cnt + 4ull * s.npairs, 256);
   s.off_entries = align_up(s.off_order + 4ull * s.npairs, 256);
   s.off_status = align_up(s.off_entries + 4ull * s.npairs * s.cap, 256);
-  s.total = align_up(s.off_status + (size_t)s.npairs * s.cap, 256);
+  s.off_desc = align_up(s.off_status + (size_t)s.npairs * s.cap, 256);
+  s.total = align_up(s.off_desc + 8ull * s.npairs * s.cap, 256);
   return s;
 }
 
@@ -84,7 +86,8 @@ PlanView plan_view(void* ws, int N, int A) {
                   reinterpret_cast<int32_t*>(b + s.off_cnt),
                   reinterpret_cast<int32_t*>(b + s.off_order),
                   reinterpret_cast<int32_t*>(b + s.off_entries),
-                  reinterpret_cast<uint8_t*>(b + s.off_status), s.cap, s.npairs};
+                  reinterpret_cast<uint8_t*>(b + s.off_status),
+                  reinterpret_cast<uint2*>(b + s.off_desc), s.cap, s.npairs};
 }
 
 // ------------------------------------------------------------- plan kernels
@@ -192,6 +195,37 @@ __global__ void plan_order_kernel(PlanView pv) {
   }
 }
 
+// Per listed tile of every pair, the facts the softmax needs to build its live
+// bits without touching the permutation: x = original index j0 of the tile's first
+// column; y = dj (bits 0-15; the original indices are j0 + c*dj when they form a
+// progression), log2(dj) (bits 16-19) when dj is a power of two (bit 20),
+// progression flag (bit 21), and the two halves' status (bits 24-27).
+__global__ void __launch_bounds__(kPlanThreads)
+plan_desc_kernel(PlanView pv, const int32_t* __restrict__ perm_kv, int A) {
+  const int p = blockIdx.x;
+  const int cnt = pv.pair_cnt[p];
+  const int32_t* ent = pv.entries + (size_t)p * pv.cap;
+  const uint8_t* sts = pv.status + (size_t)p * pv.cap;
+  uint2* desc = pv.desc + (size_t)p * pv.cap;
+  for (int e = threadIdx.x; e < cnt; e += kPlanThreads) {
+    const int row0 = ent[e] * A;
+    int j0 = row0, dj = 1;
+    bool ap = true;
+    if (perm_kv) {
+      j0 = perm_kv[row0];
+      dj = A >= 2 ? perm_kv[row0 + 1] - j0 : 1;
+      ap = dj >= 1 && dj <= 0xffff;
+      for (int c = 2; c < A && ap; ++c) ap = perm_kv[row0 + c] == j0 + c * dj;
+      if (!ap) dj = 0;
+    }
+    uint32_t y = (uint32_t)dj & 0xffffu;
+    if (ap && (dj & (dj - 1)) == 0) y |= ((uint32_t)(31 - __clz(dj)) << 16) | (1u << 20);
+    if (ap) y |= 1u << 21;
+    y |= (uint32_t)(sts[e] & 0xf) << 24;
+    desc[e] = make_uint2((uint32_t)j0, y);
+  }
+}
+
 // ------------------------------------------------------------- forward kernel
 struct FwdParams {
   int BH, N, A;
@@ -219,8 +253,7 @@ struct Smem {
   //           item_empty[2] kv_full[S] kv_empty[S]
   static constexpr int kNumBars = 15 + 2 * kSlots;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
-  static constexpr int kColOff = (kMiscOff + 16 + 15) & ~15;  // per-warp column coords [8][128]
-  static constexpr int kBytes = kColOff + 8 * 128 * 4;
+  static constexpr int kBytes = kMiscOff + 32;
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
 };
 
@@ -289,44 +322,46 @@ __device__ __forceinline__ uint32_t range_bits(int lo, int hi, int base) {
 // union of at most two ranges of c, and a lattice term (d % m == 0) is constant
 // over the segment when m divides dj.  Returns false when it is not (the caller
 // then evaluates element by element).
-__device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, int dj, int base,
-                                                 int len, uint32_t& out) {
-  const int cz = floordiv(e, dj);                       // d >= 0  <=>  c <= cz
+__device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, int dj, int sh,
+                                                 int base, int len, uint32_t& out) {
+  // floor(a / dj): an arithmetic shift when dj is a power of two (sh >= 0)
+  auto fdiv = [&](int a) { return sh >= 0 ? (a >> sh) : floordiv(a, dj); };
+  const int cz = fdiv(e);                               // d >= 0  <=>  c <= cz
   int lo1 = 0, hi1 = -1, lo2 = 0, hi2 = -1;
   bool lattice = false;
   if (p.mod > 0) {
-    if (dj % p.mod) return false;
-    lattice = (((e % p.mod) + p.mod) % p.mod) == 0;
+    if (!divisible(dj, p.mod, p.inv_mod)) return false;
+    lattice = e >= 0 && divisible(e, p.mod, p.inv_mod);   // only e >= 0 can reach c <= cz
   }
   switch (p.kind) {
     case PA_CAUSAL:
       hi1 = cz;
       break;
     case PA_WINDOW:                                     // d < p0 <=> c > (e - p0) / dj
-      lo1 = floordiv(e - p.p0, dj) + 1;
+      lo1 = fdiv(e - p.p0) + 1;
       hi1 = cz;
       break;
     case PA_DILATED:
       hi1 = lattice ? cz : -1;
       break;
     case PA_LOCAL_STRIDED:
-      lo1 = floordiv(e - p.p0, dj) + 1;
+      lo1 = fdiv(e - p.p0) + 1;
       hi1 = cz;
       hi2 = lattice ? cz : -1;
       break;
     case PA_TWOBAND:
-      lo1 = floordiv(e - p.p0, dj) + 1;
+      lo1 = fdiv(e - p.p0) + 1;
       hi1 = cz;
-      lo2 = floordiv(e - p.p1 - p.p2, dj) + 1;
-      hi2 = min(cz, floordiv(e - p.p1, dj));
+      lo2 = fdiv(e - p.p1 - p.p2) + 1;
+      hi2 = min(cz, fdiv(e - p.p1));
       break;
     case PA_SINKS:                                      // kv < p1 <=> c <= (p1 - j0 - 1) / dj
-      lo1 = floordiv(e - p.p0, dj) + 1;
+      lo1 = fdiv(e - p.p0) + 1;
       hi1 = cz;
-      hi2 = min(cz, floordiv(p.p1 - j0 - 1, dj));
+      hi2 = min(cz, fdiv(p.p1 - j0 - 1));
       break;
     case PA_FAR_STRIDED:                                // d >= p0 <=> c <= (e - p0) / dj
-      hi1 = lattice ? min(cz, floordiv(e - p.p0, dj)) : -1;
+      hi1 = lattice ? min(cz, fdiv(e - p.p0)) : -1;
       break;
     default:
       return false;
@@ -338,13 +373,13 @@ __device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, i
 }
 
 // Live bits of `n` (<= 32) columns evaluated one by one; column c has original
-// index cols[c] when given, else j0 + (base + c) * dj.
+// index cols[c] (global memory) when given, else j0 + (base + c) * dj.
 __device__ __forceinline__ uint32_t element_bits(const Pred& p, int i, const int* cols, int j0,
                                                  int dj, int base, int n) {
   uint32_t w = 0;
 #pragma unroll 1
   for (int c = 0; c < n; ++c) {
-    const int j = cols ? cols[c] : j0 + (base + c) * dj;
+    const int j = cols ? __ldg(cols + c) : j0 + (base + c) * dj;
     w |= (uint32_t)pred_live(p, i, j) << c;
   }
   return w;
@@ -403,7 +438,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
   volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
-  int* colbuf = reinterpret_cast<int*>(smem + SM::kColOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int32_t* err = P.pv.err;
@@ -623,7 +657,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + h * 128;
     const uint32_t tO = tmem + lane_off + 256 + h * D;
-    int* mycols = colbuf + warp * 128;
     uint32_t ts = 0, to = 0;
     const float c2 = P.scale_log2;
     uint32_t ring = 0;
@@ -641,59 +674,35 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       const int cnt = __ldg(P.pv.pair_cnt + p);
       const int nsup = num_super<L>(P, cnt);
       const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
-      const uint8_t* sts = P.pv.status + (size_t)p * P.pv.cap;
+      const uint2* desc = P.pv.desc + (size_t)p * P.pv.cap;
       const int row = p * 2 * BM + h * BM + r_in;
       const bool valid = row < P.N;
       const int irow = valid ? (P.perm_q ? __ldg(P.perm_q + row) : row) : -(1 << 30);
       float m_used = -INFINITY, l = 0.f;
       bool ok = true;
       for (int u = 0; u < nsup; ++u) {
-        // segments of this super-tile, as seen by this half; for partial ones the
-        // original column indices, as a progression j0 + c*dj when they form one
-        SegInfo si[S];
-        int j0s[S], djs[S];
+        // this half's view of the super-tile's segments, from the plan descriptors
+        int sts_[S], j0s[S], djs[S], shs[S], es[S], subs[S];
         bool aps[S];
 #pragma unroll
         for (int sg = 0; sg < S; ++sg) {
-          si[sg] = seg_info<L>(P, ent, sts, cnt, u, sg);
-          si[sg].st = (si[sg].st >> (2 * h)) & 3;
-          j0s[sg] = si[sg].row0;
-          djs[sg] = 1;
-          aps[sg] = true;
-        }
-        if (P.perm_kv) {
-#pragma unroll
-          for (int sg = 0; sg < S; ++sg) {
-            if (si[sg].st != 2) continue;                 // uniform across the warp
-            constexpr int PER = (L + 31) / 32;
-            int v[PER];
-            bool okp = true;
-#pragma unroll
-            for (int t = 0; t < PER; ++t) {
-              const int c = t * 32 + lane;
-              v[t] = c < L ? __ldg(P.perm_kv + si[sg].row0 + c) : 0;
-            }
-            const int j0 = __shfl_sync(0xffffffffu, v[0], 0);
-            const int dj = __shfl_sync(0xffffffffu, v[0], 1) - j0;
-#pragma unroll
-            for (int t = 0; t < PER; ++t) {
-              const int c = t * 32 + lane;
-              if (c < L) okp &= v[t] == j0 + c * dj;
-            }
-            okp = __all_sync(0xffffffffu, okp && dj >= 1);
-            j0s[sg] = j0;
-            djs[sg] = dj;
-            aps[sg] = okp;
-            if (!okp) {
-              __syncwarp();
-#pragma unroll
-              for (int t = 0; t < PER; ++t) {
-                const int c = t * 32 + lane;
-                if (c < L) mycols[sg * L + c] = v[t];
-              }
-              __syncwarp();
-            }
+          int e, sub = 0;
+          if (P.A <= BN) {
+            e = u * S + sg;
+          } else {
+            const int spt = P.A / BN;
+            e = u / spt;
+            sub = u - e * spt;
           }
+          uint2 d = make_uint2(0u, 0u);
+          if (e < cnt) d = __ldg(desc + e);
+          sts_[sg] = (d.y >> (24 + 2 * h)) & 3;
+          djs[sg] = (int)(d.y & 0xffffu);
+          shs[sg] = (d.y & (1u << 20)) ? (int)((d.y >> 16) & 15u) : -1;
+          aps[sg] = (d.y >> 21) & 1u;
+          j0s[sg] = (int)d.x + sub * BN * djs[sg];
+          es[sg] = e;
+          subs[sg] = sub;
         }
         // live bits of this row for the 128 columns, computed while S is in flight
         uint32_t mk[4];
@@ -702,13 +711,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           if constexpr (L >= 32) {
             constexpr int per = L / 32;
             const int sg = k / per, base = (k % per) * 32;
-            const int st = si[sg].st;
+            const int st = sts_[sg];
             uint32_t w = st == 1 ? 0xffffffffu : 0u;
             if (st == 2) {
-              if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg], base,
-                                                L, w)))
-                w = element_bits(P.pred, irow, aps[sg] ? nullptr : mycols + sg * L + base,
-                                 j0s[sg], djs[sg], base, 32);
+              if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg], shs[sg],
+                                                base, L, w))) {
+                const int32_t* cols = P.perm_kv ? P.perm_kv + __ldg(ent + es[sg]) * P.A +
+                                                      subs[sg] * BN + base
+                                                : nullptr;
+                w = element_bits(P.pred, irow, cols, j0s[sg], djs[sg], base, 32);
+              }
             }
             mk[k] = w;
           } else {
@@ -716,13 +728,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
 #pragma unroll
             for (int hw = 0; hw < 2; ++hw) {
               const int sg = 2 * k + hw;
-              const int st = si[sg].st;
+              const int st = sts_[sg];
               uint32_t b = st == 1 ? 0xffffu : 0u;
               if (st == 2) {
-                if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg], 0,
-                                                  L, b)))
-                  b = element_bits(P.pred, irow, aps[sg] ? nullptr : mycols + sg * L, j0s[sg],
-                                   djs[sg], 0, 16);
+                if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg],
+                                                  shs[sg], 0, L, b))) {
+                  const int32_t* cols =
+                      P.perm_kv ? P.perm_kv + __ldg(ent + es[sg]) * P.A : nullptr;
+                  b = element_bits(P.pred, irow, cols, j0s[sg], djs[sg], 0, 16);
+                }
                 b &= 0xffffu;
               }
               w |= b << (16 * hw);
@@ -1042,6 +1056,8 @@ extern "C" int pa_attn_plan(const pa_attn_args* a, void* ws, size_t ws_bytes,
                                                          a->kv_stride, a->N, a->BQ, pv);
   if ((rc = check_launch("pa_attn_plan"))) return rc;
   plan_order_kernel<<<1, 256, 0, s>>>(pv);
+  if ((rc = check_launch("pa_attn_plan"))) return rc;
+  plan_desc_kernel<<<pv.npairs, kPlanThreads, 0, s>>>(pv, a->perm_kv, a->A);
   return check_launch("pa_attn_plan");
 }
 

@@ -11,8 +11,8 @@
 //
 // The array is kNoAllocScratchBytes (4 MiB) of device memory that every GPU which
 // loads the library keeps until the process exits.  Requests whose workspace
-// would exceed it are rejected with PA_ERR_ARG (about N <= 57344 at A = 16,
-// larger for wider tiles).  All calls share the one array and each call rebuilds
+// would exceed it are rejected with PA_ERR_ARG (about N <= 36096 at A = 16,
+// 51200 at A = 32, larger for wider tiles).  All calls share the one array and each call rebuilds
 // everything in it that the kernels read, so nothing carries over between calls;
 // two calls whose work overlaps on the GPU (different streams, or several host
 // threads without ordering) race on the array and must not be issued.

@@ -45,7 +45,7 @@ class SplitPlan:
             dbi = blockindex.build_device(part.mask, N, part.BQ, part.A, perm_q=perm,
                                           perm_kv=perm, device=self.device)
             plan = attention.make_plan(dbi.kv_idx, dbi.kv_num, dbi.kv_partial, N, part.BQ,
-                                       part.A)
+                                       part.A, perm_kv=perm)
             self.perms.append(perm)
             self.indices.append(dbi)
             self.plans.append(plan)
