@@ -16,9 +16,11 @@
 // granularity while every MMA runs at N = 128.  Segments past the end of the list
 // are fetched from row N (out of bounds, zero-filled) and masked.
 //
-// Warp roles (320 threads):
+// Warp roles (384 threads):
 //   warps 0-3  softmax, half 0 (TMEM lanes 0-127)    warps 4-7  softmax, half 1
 //   warp 8     TMA producer (Q tiles, K/V ring)      warp 9     MMA issuer, TMEM owner
+//   warps 10-11 idle; they complete the third warpgroup so its registers can be
+//   handed to the softmax warpgroups (setmaxnreg)
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256, 256+D), O1 [256+D, 256+2D).
 // P (16-bit) is written by the softmax warps into columns [64,128) of its S buffer
 // and consumed from TMEM by the P.V MMA.  Per KV super-tile j the MMA warp issues,
@@ -38,7 +40,9 @@
 namespace pa {
 namespace {
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;      // three warpgroups; warps 10-11 complete the third
+constexpr int kSoftmaxRegs = 200;  // setmaxnreg split of the 384 x 168 launch registers:
+constexpr int kOtherRegs = 104;    //   256 x 200 + 128 x 104 = 64512
 constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int BM = 128;   // query rows per half
@@ -253,7 +257,8 @@ struct Smem {
   //           item_empty[2] kv_full[S] kv_empty[S]
   static constexpr int kNumBars = 15 + 2 * kSlots;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
-  static constexpr int kBytes = kMiscOff + 32;
+  static constexpr int kEpiOff = (kMiscOff + 32 + 127) & ~127;   // [8 warps][32 rows][128 B]
+  static constexpr int kBytes = kEpiOff + 8 * 32 * 128;
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
 };
 
@@ -438,6 +443,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
   volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
+  uint8_t* sEpi = smem + SM::kEpiOff;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int32_t* err = P.pv.err;
@@ -477,6 +483,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   const uint32_t tmem = *s_tmem;
 
 
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -570,23 +578,27 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         tc_fence_after();
         return r;
       };
+      // Descriptors are built once per operand tile; stepping K only moves the
+      // start-address field (bits 0-13, in 16-byte units), a compile-time offset.
+      const uint64_t q_desc[2] = {smem_desc_sw128(sQa, 16),
+                                  smem_desc_sw128(sQa + SM::kTileBytes, 16)};
       auto issue_s = [&](int h, uint32_t kslot) {
         const uint32_t d = tmem + h * 128;
-        const uint32_t qa = sQa + h * SM::kTileBytes, ka = sKVa + kslot * SM::kTileBytes;
+        const uint64_t qd = q_desc[h];
+        const uint64_t kd = smem_desc_sw128(sKVa + kslot * SM::kTileBytes, 16);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kRegion + (kk & 3) * 32;
-          mma_ss(d, smem_desc_sw128(qa + off, 16), smem_desc_sw128(ka + off, 16), P.idesc_qk,
-                 kk > 0);
+          const uint64_t off = ((kk >> 2) * kRegion + (kk & 3) * 32) >> 4;
+          mma_ss(d, qd + off, kd + off, P.idesc_qk, kk > 0);
         }
       };
       auto issue_pv = [&](int h, uint32_t vslot, bool acc) {
         const uint32_t d = tmem + 256 + h * D;
         const uint32_t pa_ = tmem + h * 128 + 64;
-        const uint32_t va = sKVa + vslot * SM::kTileBytes;
+        const uint64_t vd = smem_desc_sw128(sKVa + vslot * SM::kTileBytes, kRegion);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
-          mma_ts(d, pa_ + kk * 8, smem_desc_sw128(va + kk * 16 * 128, kRegion), P.idesc_pv,
+          mma_ts(d, pa_ + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), P.idesc_pv,
                  (acc || kk > 0) ? 1u : 0u);
       };
       auto wait_p = [&](int h) -> bool {
@@ -649,7 +661,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
       }
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ------------------------------------------------------------ softmax + epilogue
     const int h = warp >> 2;              // which half
     const int wq = warp & 3;              // TMEM lane quarter
@@ -853,36 +867,55 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           if (P.lse) P.lse[(long long)bh * P.lse_bh_stride + orw] = lse_v;
         }
       }
-      const bool store = orow != nullptr;
-      if (nsup > 0) {
+      // O leaves through a per-warp staging buffer so that every global store
+      // writes whole 128-byte row segments (8 lanes per row), including when rows
+      // are scattered by o_row_map.
+      uint8_t* stage = sEpi + warp * (32 * 128);
+      const bool have_o = nsup > 0;
+      if (have_o) {
         ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
         ++to;
         if (!__all_sync(0xffffffffu, ok)) break;
         tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < D / 32; ++k) {
-          uint32_t r[32];
-          tmem_ld32(tO + k * 32, r);
-          tmem_wait_ld();
-          tmem_regs_ready(r);
-          if (store) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + k * 64);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint4 w;
-              w.x = pack2<kBf16>(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
-              w.y = pack2<kBf16>(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
-              w.z = pack2<kBf16>(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
-              w.w = pack2<kBf16>(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
-              dst[v] = w;
-            }
-          }
-        }
-        tc_fence_before();
-      } else if (store) {
-        uint4* dst = reinterpret_cast<uint4*>(orow);
-        for (int v = 0; v < D / 8; ++v) dst[v] = make_uint4(0, 0, 0, 0);
       }
+#pragma unroll
+      for (int dh = 0; dh < D / 64; ++dh) {
+        uint32_t w[32];   // 64 outputs of this row, packed in pairs
+        if (have_o) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tO + dh * 64, r0);
+          tmem_ld32(tO + dh * 64 + 32, r1);
+          tmem_wait_ld();
+          tmem_regs_ready(r0);
+          tmem_regs_ready(r1);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            w[i] = pack2<kBf16>(__uint_as_float(r0[2 * i]) * inv_l,
+                                __uint_as_float(r0[2 * i + 1]) * inv_l);
+            w[16 + i] = pack2<kBf16>(__uint_as_float(r1[2 * i]) * inv_l,
+                                     __uint_as_float(r1[2 * i + 1]) * inv_l);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = 0u;
+        }
+        __syncwarp();   // the previous round's readers are done with the buffer
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+              make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        __syncwarp();
+        const int c = lane & 7;
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int rr = it * 4 + (lane >> 3);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+          const unsigned long long dst =
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
+          if (dst) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + dh * 128 + c * 16) = v;
+        }
+      }
+      if (have_o) tc_fence_before();
     }
   }
 
