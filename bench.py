@@ -8,10 +8,12 @@ Metric: effective TFLOP/s over LIVE mask elements,
 (configs[1]): dilated-4 mask, class A residue-4 permutation, 128x32 tiles,
 B1 H16 N8192 D128, bf16, ~N(0,1) synthetic inputs.
 
-One step = one pass of the hot path over one batch resident in HBM: the residue
-permutation of Q, K, V (one launch) and the block-sparse attention with LSE,
-whose epilogue writes O/LSE back in original row order (fused inverse
-permutation).  The block index and the forward's work list depend on the mask
+One step = one pass of the hot path over one batch resident in HBM, inputs and
+outputs in original row order: the block-sparse attention with LSE over the class A
+residue permutation, which the kernel applies on the fly (strided tensor maps read
+the permuted order; the epilogue writes rows back in original order), so no copy of
+Q, K, V is made.  The explicit permutation kernel is timed on its own
+(``permute``: GB/s of Q, K, V gathered in one launch).  The block index and the forward's work list depend on the mask
 only; they are built once per mask (as the reference builds its BlockIndex
 offline) and their time is reported separately (``index_ms``).
 
@@ -177,34 +179,25 @@ class Pipeline:
             dbi = blockindex.build_device(masks_gpu.numpy_mask(name), N, BQ, A,
                                           perm_q=self.perm, perm_kv=self.perm, device=device)
             self.plan = attention.make_plan(dbi.kv_idx, dbi.kv_num, dbi.kv_partial, N, BQ, A,
-                                            perm_kv=self.perm)
+                                            residue_stride=s)
             self.dbi = dbi
         torch.cuda.synchronize(device)
         self.index_ms = (time.perf_counter() - t0) * 1e3
 
     def launches_per_step(self):
         if self.split is not None:
-            return 1 + 1 + 1 + 1     # attention (window), gather, attention (lattice), merge
-        return 2 if self.perm is not None else 1
+            return 3                 # attention (window), attention (lattice), merge
+        return 1
 
     def step(self, q, k, v, o=None, lse=None):
-        from polyhedral_b200 import attention, permute
+        from polyhedral_b200 import attention
         if self.split is not None:
             return self.split.run(q, k, v)
-        if self.perm is not None:
-            q, k, v = permute.apply_perm_many((q, k, v), self.perm)
         return attention.block_sparse_attention(
-            q, k, v, None, None, None, *self.spec, self.BQ, self.A, perm_q=self.perm,
-            perm_kv=self.perm, o_row_map=self.perm, plan=self.plan, return_lse=True,
-            out=o, lse_out=lse)
+            q, k, v, None, None, None, *self.spec, self.BQ, self.A, residue_stride=self.s,
+            plan=self.plan, return_lse=True, out=o, lse_out=lse)
 
-    def attn_only(self, q, k, v, o, lse):
-        """The dominant kernel alone (inputs already in kernel order)."""
-        from polyhedral_b200 import attention
-        return attention.block_sparse_attention(
-            q, k, v, None, None, None, *self.spec, self.BQ, self.A, perm_q=self.perm,
-            perm_kv=self.perm, o_row_map=self.perm, plan=self.plan, return_lse=True,
-            out=o, lse_out=lse)
+    attn_only = step
 
 
 def make_inputs(wl, device, seed_offset=0, generator_device="cuda"):
@@ -270,22 +263,38 @@ def run_ours(args, rank, world, device):
 
     # dominant kernel alone, CUDA events on the launching stream
     kernel_ms = None
+    reps = max(args.steps, 20)
     if pipe.split is None:
-        from polyhedral_b200 import permute
-        kin = [permute.apply_perm_many(bufs[i], pipe.perm) if pipe.perm is not None else bufs[i]
-               for i in range(nbuf)]
-        torch.cuda.synchronize(device)
-        reps = max(args.steps, 20)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         for i in range(3):
-            pipe.attn_only(*kin[i % nbuf], *outs[i % nbuf])
+            pipe.attn_only(*bufs[i % nbuf], *outs[i % nbuf])
         e0.record()
         for i in range(reps):
-            pipe.attn_only(*kin[i % nbuf], *outs[i % nbuf])
+            pipe.attn_only(*bufs[i % nbuf], *outs[i % nbuf])
         e1.record()
         torch.cuda.synchronize(device)
         kernel_ms = e0.elapsed_time(e1) / reps
-        del kin
+
+    # the explicit class A gather (Q, K, V in one launch), HBM-bound
+    perm_line = None
+    if s:
+        from polyhedral_b200 import permute
+        pv = permute.residue_perm_device(N, s, device)
+        pouts = [permute.apply_perm_many(bufs[i], pv) for i in range(nbuf)]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            permute._permute(list(bufs[i % nbuf]), pv, scatter=False, outs=pouts[i % nbuf])
+        e1.record()
+        torch.cuda.synchronize(device)
+        pms = e0.elapsed_time(e1) / reps
+        pbytes = 2 * 3 * B * H * N * D * 2
+        _, _, hbm_peak, hbm_kind = _peaks()
+        perm_line = {"kernel": "permute_rows_kernel (Q, K, V gather)", "ms": round(pms, 5),
+                     "bytes": pbytes, "gbs": round(pbytes / (pms * 1e-3) / 1e9, 1),
+                     "frac_of_hbm": round(pbytes / (pms * 1e-3) / 1e9 / hbm_peak, 4),
+                     "peak_source": f"{hbm_kind} HBM copy"}
+        del pouts
 
     # end to end through the public API with host buffers (rank-local)
     e2e = None
@@ -341,13 +350,15 @@ def run_ours(args, rank, world, device):
                        "live_elements_per_head": live, "live_gflop_per_step_per_gpu": round(flops / 1e9, 3),
                        "l2": f"inputs rotated over {nbuf} buffer sets ({nbuf * step_bytes >> 20} MiB >= 2x L2)",
                        "index_ms": round(pipe.index_ms, 3),
-                       "step": "residue permutation of Q,K,V + attention (O, LSE) with fused inverse permutation"
-                               if wl != "c5" else "window part + gather + lattice part + LSE merge"},
+                       "step": "attention (O, LSE) over the residue permutation applied on the fly, "
+                               "inputs/outputs in original order" if wl != "c5" else
+                               "window part + lattice part (residue-16 on the fly) + LSE merge"},
             "pct_bf16_peak": round(value / world / peak, 4),
             "gpu_launches": pipe.launches_per_step() * args.steps,
             "clocks": clk.summary(),
             "e2e": e2e,
             "roofline": roof,
+            "permute": perm_line,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

@@ -68,7 +68,7 @@ typedef struct pa_pred {
 
 /* Message of the last failed call on this host thread ("" if none). */
 PA_API const char* pa_last_error(void);
-/* ABI revision of this header; bumped on any incompatible change. */
+/* ABI revision of this header (2); bumped on any incompatible change. */
 PA_API int pa_abi_version(void);
 
 /* ------------------------------------------------------------ block index
@@ -150,6 +150,16 @@ typedef struct pa_attn_args {
                                         o_row_map[r] (fuses the inverse permutation) */
   pa_pred pred;
   float scale;                       /* softmax scale; <= 0 means D^-0.5 */
+  int32_t residue_stride;            /* 0: q/k/v are in kernel order (as the reference).
+                                        s >= 1: q/k/v/o/lse are in ORIGINAL row order and the
+                                        kernel works on the residue permutation by s
+                                        (gpu/permute.py:12-16) without a copy: its row p
+                                        reads original row (p mod N/s)*s + p div (N/s), the
+                                        predicate uses those original coordinates, O/LSE
+                                        rows go back to original order; perm_q, perm_kv and
+                                        o_row_map must be NULL and N/s must be a multiple of
+                                        128 and of A.  The block index is that of the
+                                        permuted mask, as with physically permuted inputs. */
 } pa_attn_args;
 
 /* Bytes of device workspace pa_attn_plan / pa_attn_fwd need for these arguments

@@ -13,7 +13,10 @@ Extensions (keyword-only): ``return_lse`` returns (o, lse) with lse [BH, N] fp32
 result at ``o_row_map[r]`` (pass ``perm_q`` to get O back in original order, fusing
 the inverse permutation); ``plan`` reuses a work list built once by ``make_plan``;
 ``out`` / ``lse_out`` supply output buffers; ``check`` synchronises and raises if
-the kernel reported a device-side failure.  The reference's class-B emulation
+the kernel reported a device-side failure; ``residue_stride=s`` takes q, k, v (and
+returns o, lse) in ORIGINAL row order and runs on their residue permutation by s
+without copying them (the kernel's tensor maps read row p of the permuted order
+directly; the block index is still that of the permuted mask).  The reference's class-B emulation
 knobs (``gather_kv``, ``gather_mult``, ``gather_scatter``) are rejected when set;
 ``num_warps`` / ``num_stages`` are accepted and ignored.
 """
@@ -35,14 +38,17 @@ class AttnPlan:
     tile, ordered longest first.  Reusable by every forward on the same index and
     ``perm_kv``."""
 
-    def __init__(self, kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=None, device=None):
+    def __init__(self, kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=None, device=None,
+                 residue_stride=0):
         device = device or kv_num.device
         self.N, self.BQ, self.A = int(N), int(BQ), int(A)
+        self.residue_stride = int(residue_stride)
         self.kv_idx, self.kv_num, self.kv_partial = kv_idx, kv_num, kv_partial
         self.kv_stride = int(kv_idx.shape[1]) if kv_idx.dim() == 2 else 0
         self.perm_kv = _perm(perm_kv, N, device)
         a = _args_skeleton(N, BQ, A, kv_idx, kv_num, kv_partial, self.kv_stride)
         a.perm_kv = _ptr(self.perm_kv)
+        a.residue_stride = self.residue_stride
         nbytes = _lib.load().pa_attn_workspace_size(ctypes.byref(a))
         self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
         _lib.call("pa_attn_plan", ctypes.byref(a), self.workspace.data_ptr(), nbytes,
@@ -74,13 +80,13 @@ def _args_skeleton(N, BQ, A, kv_idx, kv_num, kv_partial, kv_stride):
     return a
 
 
-def make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=None):
+def make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=None, residue_stride=0):
     """Build the forward's work list once for a block index (and the K/V
-    permutation the forward will be given, if any)."""
+    permutation, explicit or residue, the forward will be given, if any)."""
     return AttnPlan(_index_tensor(kv_idx, torch.int32, kv_num.device),
                     _index_tensor(kv_num, torch.int32, kv_num.device),
                     _index_tensor(kv_partial, torch.int8, kv_num.device), N, BQ, A,
-                    perm_kv=perm_kv)
+                    perm_kv=perm_kv, residue_stride=residue_stride)
 
 
 def _index_tensor(t, dtype, device):
@@ -105,7 +111,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
                            gather_mult=1, gather_scatter=True,
                            num_warps=4, num_stages=2, *, return_lse=False,
                            o_row_map=None, plan=None, out=None, lse_out=None,
-                           check=False):
+                           check=False, residue_stride=0):
     """q, k, v: [BH, N, D] (bf16 or fp16, D in {64, 128}), on one CUDA device.
     Returns o [BH, N, D] (same dtype), or (o, lse) with ``return_lse``."""
     if gather_kv or gather_mult != 1:
@@ -123,15 +129,22 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
         if t.stride(2) != 1:
             raise ValueError(f"{name}: last dimension must be contiguous")
     dev = q.device
+    residue_stride = int(residue_stride or 0)
+    if residue_stride and (perm_q is not None or perm_kv is not None or o_row_map is not None):
+        raise ValueError("residue_stride implies the permutation; pass no perm_q, perm_kv "
+                         "or o_row_map with it")
     pq = _perm(perm_q, N, dev)
     pk = _perm(perm_kv, N, dev) if perm_kv is not None else pq
     rmap = _perm(o_row_map, N, dev)
 
     if plan is None:
-        plan = make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=pk)
+        plan = make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=pk,
+                         residue_stride=residue_stride)
     else:
         if (plan.N, plan.BQ, plan.A) != (N, BQ, A):
             raise ValueError("plan was built for a different (N, BQ, A)")
+        if plan.residue_stride != residue_stride:
+            raise ValueError("plan was built for a different residue_stride")
         if (plan.perm_kv is None) != (pk is None) or (
                 pk is not None and plan.perm_kv.data_ptr() != pk.data_ptr()
                 and not torch.equal(plan.perm_kv, pk)):
@@ -160,6 +173,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     a.perm_q, a.perm_kv, a.o_row_map = _ptr(pq), _ptr(pk), _ptr(rmap)
     a.pred = _lib.PaPred(int(kind), int(p0), int(p1), int(p2))
     a.scale = float(scale) if scale else 0.0
+    a.residue_stride = residue_stride
     ws = plan.workspace
     _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
               _lib.stream_handle(dev))

@@ -1,0 +1,827 @@
+// Shared pieces of the block-sparse attention forward: constants, the plan
+// layout, the kernel parameters and the kernel template itself.  csrc/attn.cu holds
+// the plan kernels, argument checks and C entry points; the kernel's instantiations
+// are spread over csrc/attn_k*.cu so they compile in parallel.
+#pragma once
+#include <cuda.h>
+#include <math.h>
+#include "common.cuh"
+#include "capi_util.h"
+
+namespace pa {
+namespace attn {
+
+
+constexpr int kThreads = 384;      // three warpgroups; warps 10-11 complete the third
+constexpr int kSoftmaxRegs = 200;  // setmaxnreg split of the 384 x 168 launch registers:
+constexpr int kOtherRegs = 104;    //   256 x 200 + 128 x 104 = 64512
+constexpr int kLoadWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int BM = 128;   // query rows per half
+constexpr int BN = 128;   // KV rows per super-tile
+constexpr int kTmemCols = 512;
+constexpr uint32_t kDrainLimitNs = 200u * 1000u * 1000u;
+
+// ----------------------------------------------------------------- plan layout
+struct PlanView {
+  int32_t* err;        // status word
+  int32_t* sched;      // [2]: next work item, CTAs finished (reset by the last CTA)
+  int32_t* pair_cnt;   // [npairs] union entries of pair p
+  int32_t* order;      // [npairs] pairs sorted by decreasing entry count
+  int32_t* entries;    // [npairs * cap] ascending A-tile ids
+  uint8_t* status;     // [npairs * cap] bits 0-1 half 0, bits 2-3 half 1: 0 dead 1 full 2 partial
+  uint2* desc;         // [npairs * cap] per listed tile: see make_desc below
+  int cap;
+  int npairs;
+};
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct PlanSizes {
+  size_t off_cnt, off_order, off_entries, off_status, off_desc, total;
+  int cap, npairs;
+};
+
+inline PlanSizes plan_sizes(int N, int A) {
+  PlanSizes s;
+  s.npairs = (N + 2 * BM - 1) / (2 * BM);
+  s.cap = N / A;
+  s.off_cnt = 256;
+  s.off_order = align_up(s.off_cnt + 4ull * s.npairs, 256);
+  s.off_entries = align_up(s.off_order + 4ull * s.npairs, 256);
+  s.off_status = align_up(s.off_entries + 4ull * s.npairs * s.cap, 256);
+  s.off_desc = align_up(s.off_status + (size_t)s.npairs * s.cap, 256);
+  s.total = align_up(s.off_desc + 8ull * s.npairs * s.cap, 256);
+  return s;
+}
+
+inline PlanView plan_view(void* ws, int N, int A) {
+  const PlanSizes s = plan_sizes(N, A);
+  char* b = static_cast<char*>(ws);
+  return PlanView{reinterpret_cast<int32_t*>(b), reinterpret_cast<int32_t*>(b + 64),
+                  reinterpret_cast<int32_t*>(b + s.off_cnt),
+                  reinterpret_cast<int32_t*>(b + s.off_order),
+                  reinterpret_cast<int32_t*>(b + s.off_entries),
+                  reinterpret_cast<uint8_t*>(b + s.off_status),
+                  reinterpret_cast<uint2*>(b + s.off_desc), s.cap, s.npairs};
+}
+
+// ------------------------------------------------------------- plan kernels
+// ------------------------------------------------------------- forward kernel
+struct FwdParams {
+  int BH, N, A;
+  int rs, nb;          // residue stride of a virtual permutation (0 = none), N / rs
+  const int32_t* perm_q;
+  const int32_t* perm_kv;
+  const int32_t* o_row_map;
+  void* o;
+  float* lse;
+  long long o_bh_stride, o_row_stride, lse_bh_stride;
+  Pred pred;
+  float scale_log2;
+  PlanView pv;
+  uint32_t idesc_qk, idesc_pv;
+  int total_items;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int kTileBytes = BM * D * 2;               // one 128-row tile, 16-bit
+  static constexpr int kSlots = D == 128 ? 4 : 8;
+  static constexpr int kQOff = 0;
+  static constexpr int kKVOff = 2 * kTileBytes;
+  static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
+  // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] drain item_full[2]
+  //           item_empty[2] kv_full[S] kv_empty[S]
+  static constexpr int kNumBars = 15 + 2 * kSlots;
+  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
+  static constexpr int kEpiOff = (kMiscOff + 32 + 127) & ~127;   // [8 warps][32 rows][128 B]
+  static constexpr int kBytes = kEpiOff + 8 * 32 * 128;
+  static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kBf16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Number of super-tiles of pair `p` and, for segment `sg` of super-tile `u`, the
+// first KV row (N when past the end) and the 4-bit status.
+struct SegInfo {
+  int row0;
+  int st;
+};
+
+template <int L>
+__device__ __forceinline__ int num_super(const FwdParams& P, int cnt) {
+  constexpr int S = BN / L;
+  if (P.A <= BN) return (cnt + S - 1) / S;
+  return cnt * (P.A / BN);
+}
+
+template <int L>
+__device__ __forceinline__ SegInfo seg_info(const FwdParams& P, const int32_t* ent,
+                                            const uint8_t* sts, int cnt, int u, int sg) {
+  constexpr int S = BN / L;
+  if (P.A <= BN) {
+    const int e = u * S + sg;
+    if (e < cnt) return SegInfo{__ldg(ent + e) * P.A, (int)__ldg(sts + e)};
+    return SegInfo{P.N, 0};
+  }
+  const int sub = P.A / BN;
+  const int e = u / sub;
+  return SegInfo{__ldg(ent + e) * P.A + (u - e * sub) * BN, (int)__ldg(sts + e)};
+}
+
+// floor(a / b) for b > 0
+__device__ __forceinline__ int floordiv(int a, int b) {
+  return a >= 0 ? a / b : -((-a + b - 1) / b);
+}
+
+// Bits (c - base) for c in [lo, hi], clipped to the word [base, base + 32).
+__device__ __forceinline__ uint32_t range_bits(int lo, int hi, int base) {
+  lo = max(lo - base, 0);
+  hi = min(hi - base, 31);
+  if (hi < lo) return 0u;
+  const uint32_t upto = hi == 31 ? 0xffffffffu : ((2u << hi) - 1u);
+  return upto & ~((1u << lo) - 1u);
+}
+
+// Live bits of columns [base, base + 32) of a segment of `len` columns whose
+// original indices form the progression j0 + c*dj (dj >= 1), for the row with
+// original index i = j0 + e.  With d = e - c*dj decreasing in c, every kind is a
+// union of at most two ranges of c, and a lattice term (d % m == 0) is constant
+// over the segment when m divides dj.  Returns false when it is not (the caller
+// then evaluates element by element).
+__device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, int dj, int sh,
+                                                 int base, int len, uint32_t& out) {
+  // floor(a / dj): an arithmetic shift when dj is a power of two (sh >= 0)
+  auto fdiv = [&](int a) { return sh >= 0 ? (a >> sh) : floordiv(a, dj); };
+  const int cz = fdiv(e);                               // d >= 0  <=>  c <= cz
+  int lo1 = 0, hi1 = -1, lo2 = 0, hi2 = -1;
+  bool lattice = false;
+  if (p.mod > 0) {
+    if (!divisible(dj, p.mod, p.inv_mod)) return false;
+    lattice = e >= 0 && divisible(e, p.mod, p.inv_mod);   // only e >= 0 can reach c <= cz
+  }
+  switch (p.kind) {
+    case PA_CAUSAL:
+      hi1 = cz;
+      break;
+    case PA_WINDOW:                                     // d < p0 <=> c > (e - p0) / dj
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      break;
+    case PA_DILATED:
+      hi1 = lattice ? cz : -1;
+      break;
+    case PA_LOCAL_STRIDED:
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      hi2 = lattice ? cz : -1;
+      break;
+    case PA_TWOBAND:
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      lo2 = fdiv(e - p.p1 - p.p2) + 1;
+      hi2 = min(cz, fdiv(e - p.p1));
+      break;
+    case PA_SINKS:                                      // kv < p1 <=> c <= (p1 - j0 - 1) / dj
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      hi2 = min(cz, fdiv(p.p1 - j0 - 1));
+      break;
+    case PA_FAR_STRIDED:                                // d >= p0 <=> c <= (e - p0) / dj
+      hi1 = lattice ? min(cz, fdiv(e - p.p0)) : -1;
+      break;
+    default:
+      return false;
+  }
+  hi1 = min(hi1, len - 1);
+  hi2 = min(hi2, len - 1);
+  out = range_bits(lo1, hi1, base) | range_bits(lo2, hi2, base);
+  return true;
+}
+
+// Live bits of `n` (<= 32) columns evaluated one by one; column c has original
+// index cols[c] (global memory) when given, else j0 + (base + c) * dj.
+__device__ __forceinline__ uint32_t element_bits(const Pred& p, int i, const int* cols, int j0,
+                                                 int dj, int base, int n) {
+  uint32_t w = 0;
+#pragma unroll 1
+  for (int c = 0; c < n; ++c) {
+    const int j = cols ? __ldg(cols + c) : j0 + (base + c) * dj;
+    w |= (uint32_t)pred_live(p, i, j) << c;
+  }
+  return w;
+}
+
+// d = a * b + c on two lanes at once (f32x2).
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+// a += b on two lanes at once (f32x2).
+__device__ __forceinline__ void fadd2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb;\n\t"
+      "mov.b64 ra, {%0, %1};\n\t"
+      "mov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 ra, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, ra;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+template <int D, int L, bool kBf16, bool kRS>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const FwdParams P) {
+  using SM = Smem<D>;
+  constexpr int S = BN / L;              // segments per super-tile
+  constexpr int NS = SM::kSlots;
+  constexpr int kChunks = D / 64;        // 128-byte swizzle chunks along D
+  constexpr uint32_t kRegion = BM * 128; // bytes of one 64-column chunk of a 128-row tile
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem + SM::kQOff;
+  uint8_t* sKV = smem + SM::kKVOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 2;
+  uint64_t* s_full = bars + 4;
+  uint64_t* p_full = bars + 6;
+  uint64_t* o_full = bars + 8;
+  uint64_t* drain = bars + 10;
+  uint64_t* item_full = bars + 11;
+  uint64_t* item_empty = bars + 13;
+  uint64_t* kv_full = bars + 15;
+  uint64_t* kv_empty = bars + 15 + NS;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
+  volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
+  uint8_t* sEpi = smem + SM::kEpiOff;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* err = P.pv.err;
+
+  if (threadIdx.x == 0) {
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&q_full[h], 1);
+      mbar_init(&q_empty[h], 1);
+      mbar_init(&s_full[h], 1);
+      mbar_init(&p_full[h], BM);
+      mbar_init(&o_full[h], 1);
+    }
+    mbar_init(drain, 1);
+    for (int r = 0; r < 2; ++r) {
+      mbar_init(&item_full[r], 1);
+      mbar_init(&item_empty[r], 1 + 8);   // MMA thread + one lane per softmax warp
+    }
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(s_tmem, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int qi = 0;
+      int q_armed[2] = {0, 0};
+      uint32_t kv_g = 0;
+      uint32_t ring = 0;
+      while (true) {
+        // fetch the next work item and hand it to the MMA and softmax warps
+        int it = atomicAdd(P.pv.sched, 1);
+        if (it >= P.total_items || *s_abort) it = -1;
+        const uint32_t rs = ring & 1;
+        if (ring >= 2 &&
+            !mbar_wait(&item_empty[rs], ((ring >> 1) - 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM))
+          break;
+        s_item[rs] = it;
+        mbar_arrive(&item_full[rs]);
+        ++ring;
+        if (it < 0) break;
+        const int p = __ldg(P.pv.order + it / P.BH);
+        const int bh = it - (it / P.BH) * P.BH;
+        const int cnt = __ldg(P.pv.pair_cnt + p);
+        const int nsup = num_super<L>(P, cnt);
+        if (nsup == 0) continue;
+        const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
+        const uint8_t* sts = P.pv.status + (size_t)p * P.pv.cap;
+        bool ok = true;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (qi > 0) ok = mbar_wait(&q_empty[h], (qi - 1) & 1, s_abort, err, DEV_TIMEOUT_Q);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&q_full[h], SM::kTileBytes);
+          ++q_armed[h];
+          const int qr = p * 2 * BM + h * BM;
+          for (int c = 0; c < kChunks; ++c) {
+            if constexpr (kRS)
+              tma_load_4d(sQ + h * SM::kTileBytes + c * kRegion, &tm_q, &q_full[h], c * 64,
+                          qr / P.nb, qr % P.nb, bh);
+            else
+              tma_load_3d(sQ + h * SM::kTileBytes + c * kRegion, &tm_q, &q_full[h], c * 64, qr,
+                          bh);
+          }
+        }
+        if (!ok) break;
+        for (int u = 0; u < nsup && ok; ++u) {
+          SegInfo si[S];
+#pragma unroll
+          for (int sg = 0; sg < S; ++sg) si[sg] = seg_info<L>(P, ent, sts, cnt, u, sg);
+          for (int kv = 0; kv < 2; ++kv) {
+            const uint32_t slot = kv_g % NS;
+            if (kv_g >= (uint32_t)NS) {
+              ok = mbar_wait(&kv_empty[slot], ((kv_g / NS) - 1) & 1, s_abort, err,
+                             DEV_TIMEOUT_KV);
+              if (!ok) break;
+            }
+            ++kv_g;
+            uint8_t* dst = sKV + slot * SM::kTileBytes;
+            mbar_arrive_expect_tx(&kv_full[slot], SM::kTileBytes);
+            const void* tm = kv == 0 ? (const void*)&tm_k : (const void*)&tm_v;
+#pragma unroll
+            for (int sg = 0; sg < S; ++sg) {
+              const int r0 = si[sg].row0;
+              for (int c = 0; c < kChunks; ++c) {
+                if constexpr (kRS)
+                  tma_load_4d(dst + c * kRegion + sg * L * 128, tm, &kv_full[slot], c * 64,
+                              r0 / P.nb, r0 % P.nb, bh);
+                else
+                  tma_load_3d(dst + c * kRegion + sg * L * 128, tm, &kv_full[slot], c * 64, r0,
+                              bh);
+              }
+            }
+          }
+        }
+        ++qi;
+      }
+      // Teardown: let every copy this thread issued land before the CTA can exit.
+      // A phase that completed long ago also satisfies the parity test, so this
+      // only ever waits on copies still in flight.
+      const uint64_t t0 = globaltimer();
+      for (uint32_t s = 0; s < (uint32_t)NS && s < kv_g; ++s) {
+        const uint32_t uses = (kv_g - s + NS - 1) / NS;   // loads issued into slot s
+        while (!mbar_try_wait(&kv_full[s], (uses - 1) & 1)) {
+          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+        }
+      }
+      for (int h = 0; h < 2; ++h) {
+        if (q_armed[h] == 0) continue;
+        while (!mbar_try_wait(&q_full[h], (q_armed[h] - 1) & 1)) {
+          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int qi = 0;
+      uint32_t kv_c = 0;
+      uint32_t tp[2] = {0, 0};
+      bool ok = true;
+      const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
+      auto wait_kv = [&](uint32_t& slot) -> bool {
+        slot = kv_c % NS;
+        const bool r = mbar_wait(&kv_full[slot], (kv_c / NS) & 1, s_abort, err, DEV_TIMEOUT_KV);
+        ++kv_c;
+        tc_fence_after();
+        return r;
+      };
+      // Descriptors are built once per operand tile; stepping K only moves the
+      // start-address field (bits 0-13, in 16-byte units), a compile-time offset.
+      const uint64_t q_desc[2] = {smem_desc_sw128(sQa, 16),
+                                  smem_desc_sw128(sQa + SM::kTileBytes, 16)};
+      auto issue_s = [&](int h, uint32_t kslot) {
+        const uint32_t d = tmem + h * 128;
+        const uint64_t qd = q_desc[h];
+        const uint64_t kd = smem_desc_sw128(sKVa + kslot * SM::kTileBytes, 16);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t off = ((kk >> 2) * kRegion + (kk & 3) * 32) >> 4;
+          mma_ss(d, qd + off, kd + off, P.idesc_qk, kk > 0);
+        }
+      };
+      auto issue_pv = [&](int h, uint32_t vslot, bool acc) {
+        const uint32_t d = tmem + 256 + h * D;
+        const uint32_t pa_ = tmem + h * 128 + 64;
+        const uint64_t vd = smem_desc_sw128(sKVa + vslot * SM::kTileBytes, kRegion);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          mma_ts(d, pa_ + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), P.idesc_pv,
+                 (acc || kk > 0) ? 1u : 0u);
+      };
+      auto wait_p = [&](int h) -> bool {
+        const bool r = mbar_wait(&p_full[h], tp[h] & 1, s_abort, err, DEV_TIMEOUT_P);
+        ++tp[h];
+        tc_fence_after();
+        return r;
+      };
+      uint32_t ring = 0;
+      while (ok) {
+        const uint32_t rs = ring & 1;
+        if (!(ok = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM)))
+          break;
+        const int it = s_item[rs];
+        mbar_arrive(&item_empty[rs]);
+        ++ring;
+        if (it < 0) break;
+        const int p = __ldg(P.pv.order + it / P.BH);
+        const int nsup = num_super<L>(P, __ldg(P.pv.pair_cnt + p));
+        if (nsup == 0) continue;
+        ok = mbar_wait(&q_full[0], qi & 1, s_abort, err, DEV_TIMEOUT_Q) &&
+             mbar_wait(&q_full[1], qi & 1, s_abort, err, DEV_TIMEOUT_Q);
+        tc_fence_after();
+        if (!ok) break;
+        uint32_t ks, vs;
+        if (!(ok = wait_kv(ks))) break;
+        issue_s(0, ks);
+        tc_commit(&s_full[0]);
+        issue_s(1, ks);
+        tc_commit(&s_full[1]);
+        tc_commit(&kv_empty[ks]);
+        for (int u = 1; u < nsup && ok; ++u) {
+          if (!(ok = wait_kv(vs))) break;
+          if (!(ok = wait_kv(ks))) break;
+          for (int h = 0; h < 2 && ok; ++h) {
+            if (!(ok = wait_p(h))) break;
+            issue_pv(h, vs, u > 1);
+            issue_s(h, ks);
+            tc_commit(&s_full[h]);
+          }
+          tc_commit(&kv_empty[vs]);
+          tc_commit(&kv_empty[ks]);
+        }
+        if (!ok) break;
+        tc_commit(&q_empty[0]);
+        tc_commit(&q_empty[1]);
+        if (!(ok = wait_kv(vs))) break;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!(ok = wait_p(h))) break;
+          issue_pv(h, vs, nsup > 1);
+          tc_commit(&o_full[h]);
+        }
+        tc_commit(&kv_empty[vs]);
+        ++qi;
+      }
+      // drain: the commit lands once every MMA issued above has completed
+      tc_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+      }
+    }
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    // ------------------------------------------------------------ softmax + epilogue
+    const int h = warp >> 2;              // which half
+    const int wq = warp & 3;              // TMEM lane quarter
+    const int r_in = wq * 32 + lane;      // row within the half
+    const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + lane_off + h * 128;
+    const uint32_t tO = tmem + lane_off + 256 + h * D;
+    uint32_t ts = 0, to = 0;
+    const float c2 = P.scale_log2;
+    uint32_t ring = 0;
+    while (true) {
+      const uint32_t rs = ring & 1;
+      bool got = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM);
+      if (!__all_sync(0xffffffffu, got)) break;
+      const int it = s_item[rs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[rs]);
+      ++ring;
+      if (it < 0) break;
+      const int p = __ldg(P.pv.order + it / P.BH);
+      const int bh = it - (it / P.BH) * P.BH;
+      const int cnt = __ldg(P.pv.pair_cnt + p);
+      const int nsup = num_super<L>(P, cnt);
+      const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
+      const uint2* desc = P.pv.desc + (size_t)p * P.pv.cap;
+      const int row = p * 2 * BM + h * BM + r_in;
+      const bool valid = row < P.N;
+      const int irow = !valid        ? -(1 << 30)
+                       : kRS          ? (row % P.nb) * P.rs + row / P.nb
+                       : P.perm_q    ? __ldg(P.perm_q + row)
+                                     : row;
+      float m_used = -INFINITY, l = 0.f;
+      bool ok = true;
+      for (int u = 0; u < nsup; ++u) {
+        // this half's view of the super-tile's segments, from the plan descriptors
+        int sts_[S], j0s[S], djs[S], shs[S], es[S], subs[S];
+        bool aps[S];
+#pragma unroll
+        for (int sg = 0; sg < S; ++sg) {
+          int e, sub = 0;
+          if (P.A <= BN) {
+            e = u * S + sg;
+          } else {
+            const int spt = P.A / BN;
+            e = u / spt;
+            sub = u - e * spt;
+          }
+          uint2 d = make_uint2(0u, 0u);
+          if (e < cnt) d = __ldg(desc + e);
+          sts_[sg] = (d.y >> (24 + 2 * h)) & 3;
+          djs[sg] = (int)(d.y & 0xffffu);
+          shs[sg] = (d.y & (1u << 20)) ? (int)((d.y >> 16) & 15u) : -1;
+          aps[sg] = (d.y >> 21) & 1u;
+          j0s[sg] = (int)d.x + sub * BN * djs[sg];
+          es[sg] = e;
+          subs[sg] = sub;
+        }
+        // live bits of this row for the 128 columns, computed while S is in flight
+        uint32_t mk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if constexpr (L >= 32) {
+            constexpr int per = L / 32;
+            const int sg = k / per, base = (k % per) * 32;
+            const int st = sts_[sg];
+            uint32_t w = st == 1 ? 0xffffffffu : 0u;
+            if (st == 2) {
+              if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg], shs[sg],
+                                                base, L, w))) {
+                const int32_t* cols = P.perm_kv ? P.perm_kv + __ldg(ent + es[sg]) * P.A +
+                                                      subs[sg] * BN + base
+                                                : nullptr;
+                w = element_bits(P.pred, irow, cols, j0s[sg], djs[sg], base, 32);
+              }
+            }
+            mk[k] = w;
+          } else {
+            uint32_t w = 0;
+#pragma unroll
+            for (int hw = 0; hw < 2; ++hw) {
+              const int sg = 2 * k + hw;
+              const int st = sts_[sg];
+              uint32_t b = st == 1 ? 0xffffu : 0u;
+              if (st == 2) {
+                if (!(aps[sg] && progression_bits(P.pred, irow - j0s[sg], j0s[sg], djs[sg],
+                                                  shs[sg], 0, L, b))) {
+                  const int32_t* cols =
+                      P.perm_kv ? P.perm_kv + __ldg(ent + es[sg]) * P.A : nullptr;
+                  b = element_bits(P.pred, irow, cols, j0s[sg], djs[sg], 0, 16);
+                }
+                b &= 0xffffu;
+              }
+              w |= b << (16 * hw);
+            }
+            mk[k] = w;
+          }
+        }
+        ok = mbar_wait(&s_full[h], ts & 1, s_abort, err, DEV_TIMEOUT_S);
+        ++ts;
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        float s[128];
+        {
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(tS + 0, r0);
+          tmem_ld32(tS + 32, r1);
+          tmem_ld32(tS + 64, r2);
+          tmem_ld32(tS + 96, r3);
+          tmem_wait_ld();
+          tmem_regs_ready(r0);
+          tmem_regs_ready(r1);
+          tmem_regs_ready(r2);
+          tmem_regs_ready(r3);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s[i] = __uint_as_float(r0[i]);
+            s[32 + i] = __uint_as_float(r1[i]);
+            s[64 + i] = __uint_as_float(r2[i]);
+            s[96 + i] = __uint_as_float(r3[i]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (mk[k] != 0xffffffffu) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (!((mk[k] >> i) & 1u)) s[k * 32 + i] = -INFINITY;
+          }
+        }
+        float mx;
+        {
+          float m8[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) m8[j] = fmaxf(s[2 * j], s[2 * j + 1]);
+#pragma unroll
+          for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) m8[j] = fmax3(m8[j], s[c + 2 * j], s[c + 2 * j + 1]);
+          }
+          mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+        }
+        const float m_tile = mx * c2;
+        const float m_new = fmaxf(m_used, m_tile);
+        bool bump = false;
+        float factor = 1.f;
+        if (u == 0) {
+          m_used = m_new;
+        } else if (m_new > m_used + 8.0f) {
+          bump = true;
+          factor = ex2(m_used - m_new);
+          m_used = m_new;
+        }
+        const bool need_o = bump && l > 0.f;
+        if (bump) l *= factor;
+        const float msub = m_used == -INFINITY ? 0.f : m_used;
+        float r8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r8[j] = 0.f;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int c = q4 * 32 + 2 * i;
+            float x0, x1;
+            ffma2(x0, x1, s[c], s[c + 1], c2, -msub);
+            const float a = ex2(x0);
+            const float b = ex2(x1);
+            const int j = (2 * i) & 7;
+            fadd2(r8[j], r8[j + 1], a, b);
+            pk[i] = pack2<kBf16>(a, b);
+          }
+          tmem_st16(tS + 64 + q4 * 16, pk);
+        }
+        l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
+        // O rescale (rare: only when the running max grew by more than 2^8)
+        if (__any_sync(0xffffffffu, need_o)) {
+          const float f = need_o ? factor : 1.f;
+#pragma unroll 1
+          for (int k = 0; k < D / 32; ++k) {
+            uint32_t r[32];
+            tmem_ld32(tO + k * 32, r);
+            tmem_wait_ld();
+            tmem_regs_ready(r);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+            tmem_st32(tO + k * 32, r);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[h]);
+      }
+      if (!ok) break;
+      // epilogue: O / l, LSE
+      float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const float lse_v = l > 0.f ? (m_used + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+      char* orow = nullptr;
+      if (valid) {
+        const int orw = kRS          ? (row % P.nb) * P.rs + row / P.nb
+                        : P.o_row_map ? __ldg(P.o_row_map + row)
+                                      : row;
+        if ((unsigned)orw < (unsigned)P.N) {
+          orow = static_cast<char*>(P.o) +
+                 ((long long)bh * P.o_bh_stride + (long long)orw * P.o_row_stride) * 2;
+          if (P.lse) P.lse[(long long)bh * P.lse_bh_stride + orw] = lse_v;
+        }
+      }
+      // O leaves through a per-warp staging buffer so that every global store
+      // writes whole 128-byte row segments (8 lanes per row), including when rows
+      // are scattered by o_row_map.
+      uint8_t* stage = sEpi + warp * (32 * 128);
+      const bool have_o = nsup > 0;
+      if (have_o) {
+        ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
+        ++to;
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int dh = 0; dh < D / 64; ++dh) {
+        uint32_t w[32];   // 64 outputs of this row, packed in pairs
+        if (have_o) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tO + dh * 64, r0);
+          tmem_ld32(tO + dh * 64 + 32, r1);
+          tmem_wait_ld();
+          tmem_regs_ready(r0);
+          tmem_regs_ready(r1);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            w[i] = pack2<kBf16>(__uint_as_float(r0[2 * i]) * inv_l,
+                                __uint_as_float(r0[2 * i + 1]) * inv_l);
+            w[16 + i] = pack2<kBf16>(__uint_as_float(r1[2 * i]) * inv_l,
+                                     __uint_as_float(r1[2 * i + 1]) * inv_l);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) w[i] = 0u;
+        }
+        __syncwarp();   // the previous round's readers are done with the buffer
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+              make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        __syncwarp();
+        const int c = lane & 7;
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int rr = it * 4 + (lane >> 3);
+          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+          const unsigned long long dst =
+              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
+          if (dst) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + dh * 128 + c * 16) = v;
+        }
+      }
+      if (have_o) tc_fence_before();
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+  if (threadIdx.x == 0) {
+    // the last CTA to finish rewinds the work counter for the next launch
+    __threadfence();
+    if (atomicAdd(P.pv.sched + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(P.pv.sched, 0);
+      atomicExch(P.pv.sched + 1, 0);
+    }
+  }
+}
+
+
+// Launchers of one instantiation family each (head dim x residue mode), defined in
+// csrc/attn_k*.cu so the sixteen-odd kernel instantiations compile in parallel.
+using Tmap = CUtensorMap;
+#define PA_DECLARE_LAUNCH(name)                                                            \
+  int name(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P, int grid, \
+           int L, bool bf16, cudaStream_t stream);
+PA_DECLARE_LAUNCH(launch_d128)
+PA_DECLARE_LAUNCH(launch_d128_residue)
+PA_DECLARE_LAUNCH(launch_d64)
+PA_DECLARE_LAUNCH(launch_d64_residue)
+#undef PA_DECLARE_LAUNCH
+
+// Body of the launchers: pick the instantiation for (L, dtype).
+template <int D, bool kRS>
+int launch_family(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P, int grid,
+                  int L, bool bf16, cudaStream_t stream) {
+  auto go = [&](auto kernel) -> int {
+    const int smem = Smem<D>::kAlloc;
+    PA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+            "pa_attn_fwd");
+    kernel<<<grid, kThreads, smem, stream>>>(tq, tk, tv, P);
+    return PA_OK;
+  };
+  switch (L) {
+    case 16: return bf16 ? go(attn_fwd_kernel<D, 16, true, kRS>) : go(attn_fwd_kernel<D, 16, false, kRS>);
+    case 32: return bf16 ? go(attn_fwd_kernel<D, 32, true, kRS>) : go(attn_fwd_kernel<D, 32, false, kRS>);
+    case 64: return bf16 ? go(attn_fwd_kernel<D, 64, true, kRS>) : go(attn_fwd_kernel<D, 64, false, kRS>);
+    default: return bf16 ? go(attn_fwd_kernel<D, 128, true, kRS>) : go(attn_fwd_kernel<D, 128, false, kRS>);
+  }
+}
+
+}  // namespace attn
+}  // namespace pa

@@ -8,9 +8,10 @@ study (src/polyattn/experiments/compose.py:7-17: split, per-part class-A basis,
 merge), which the reference only counts.  Disjointness is required: an element in
 two parts would be counted twice in the softmax denominator.
 
-The permuted part gathers Q/K/V once into residue order, evaluates the predicate in
-original coordinates (perm_q = perm_kv = perm) and writes its O/LSE rows straight
-back to original order (o_row_map = perm), so the merge needs no row map.
+A part in a residue-permuted basis runs on Q/K/V in their original row order: the
+kernel reads the permuted order through strided tensor maps (``residue_stride``),
+evaluates the predicate in original coordinates and writes O/LSE back in original
+order, so no part copies Q/K/V and the merge needs no row map.
 """
 from dataclasses import dataclass
 from typing import Optional
@@ -45,7 +46,7 @@ class SplitPlan:
             dbi = blockindex.build_device(part.mask, N, part.BQ, part.A, perm_q=perm,
                                           perm_kv=perm, device=self.device)
             plan = attention.make_plan(dbi.kv_idx, dbi.kv_num, dbi.kv_partial, N, part.BQ,
-                                       part.A, perm_kv=perm)
+                                       part.A, residue_stride=part.stride)
             self.perms.append(perm)
             self.indices.append(dbi)
             self.plans.append(plan)
@@ -55,15 +56,9 @@ class SplitPlan:
         o = lse = None
         for i, part in enumerate(self.parts):
             kind, p0, p1, p2 = part.mask.spec
-            perm = self.perms[i]
-            if perm is None:
-                qi, ki, vi = q, k, v
-            else:
-                qi, ki, vi = permute.apply_perm_many((q, k, v), perm)
             oi, li = attention.block_sparse_attention(
-                qi, ki, vi, None, None, None, kind, p0, p1, p2, part.BQ, part.A,
-                scale=scale, perm_q=perm, perm_kv=perm, o_row_map=perm,
-                plan=self.plans[i], return_lse=True,
+                q, k, v, None, None, None, kind, p0, p1, p2, part.BQ, part.A,
+                scale=scale, residue_stride=part.stride, plan=self.plans[i], return_lse=True,
                 out=(out if (i == 0 and out is not None) else None))
             if o is None:
                 o, lse = oi, li

@@ -89,6 +89,44 @@ def test_permuted_path(name, s, BQ, A):
     assert torch.equal(of, o) and torch.equal(lf, lse)
 
 
+@pytest.mark.parametrize("name,s,N", [("dilated-4", 4, 1024), ("local64+str8", 8, 2048),
+                                      ("far1024+str16", 16, 4096), ("sinks4+win256", 2, 512)])
+@pytest.mark.parametrize("BQ,A", [(16, 16), (128, 32), (128, 128)])
+def test_residue_stride_equals_explicit_permutation(name, s, N, BQ, A):
+    """The on-the-fly residue permutation (strided tensor maps) gives exactly what
+    the explicit gather + permuted kernel + inverse scatter gives."""
+    from polyhedral_b200 import blockindex, masks, permute
+    from polyhedral_b200.triton_attn import block_sparse_attention
+    q, k, v = _rand(2, N, 128, torch.bfloat16, seed=s)
+    spec = SPECS[name]
+    perm = torch.from_numpy(permute.residue_perm(N, s)).cuda()
+    bi = blockindex.build(masks.from_spec(*spec), N, BQ, A, perm_q=perm, perm_kv=perm)
+    kvi, kvn, kvp = blockindex.to_cuda(bi)
+    qp, kp, vp = permute.apply_perm_many((q, k, v), perm)
+    o1, l1 = block_sparse_attention(qp, kp, vp, kvi, kvn, kvp, *spec, BQ, A, perm_q=perm,
+                                    perm_kv=perm, o_row_map=perm, return_lse=True, check=True)
+    o2, l2 = block_sparse_attention(q, k, v, kvi, kvn, kvp, *spec, BQ, A, residue_stride=s,
+                                    return_lse=True, check=True)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    o_ref, lse_ref = _oracle(q, k, v, name, N)
+    _assert_close(o2, l2, o_ref, lse_ref)
+
+
+def test_residue_stride_argument_errors():
+    from polyhedral_b200 import _lib, blockindex, masks, permute
+    from polyhedral_b200.triton_attn import block_sparse_attention
+    N = 1024
+    q, k, v = _rand(1, N, 128, torch.bfloat16)
+    perm = torch.from_numpy(permute.residue_perm(N, 4)).cuda()
+    bi = blockindex.build(masks.Dilated(4), N, 128, 32, perm_q=perm, perm_kv=perm)
+    kvi, kvn, kvp = blockindex.to_cuda(bi)
+    with pytest.raises(ValueError):
+        block_sparse_attention(q, k, v, kvi, kvn, kvp, 2, 4, 0, 0, 128, 32, residue_stride=4,
+                               perm_q=perm)
+    with pytest.raises(_lib.PolyattnError, match="multiple of 128"):
+        block_sparse_attention(q, k, v, kvi, kvn, kvp, 2, 4, 0, 0, 128, 32, residue_stride=16)
+
+
 def test_config1_full():
     """Configuration 1: window-128, B1 H4 N1024 D64, fp32 ~N(0,1) seed 0, cast to bf16."""
     g = torch.Generator().manual_seed(0)
@@ -180,12 +218,15 @@ def _check_sampled(o, lse, q, k, v, name, heads, rows):
 
 
 def test_config2_dilated4_rp4_full_size():
-    from polyhedral_b200 import permute
+    from polyhedral_b200 import blockindex, masks, permute
+    from polyhedral_b200.triton_attn import block_sparse_attention
     N = 8192
     q, k, v = _gpu_inputs(1, 16, N, 128, 1)
     perm = permute.residue_perm_device(N, 4)
-    qp, kp, vp = permute.apply_perm_many((q, k, v), perm)
-    o, lse = _run(qp, kp, vp, "dilated-4", N, 128, 32, perm=perm, o_row_map=perm)
+    bi = blockindex.build_device(masks.Dilated(4), N, 128, 32, perm_q=perm, perm_kv=perm)
+    o, lse = block_sparse_attention(q, k, v, bi.kv_idx, bi.kv_num, bi.kv_partial,
+                                    *SPECS["dilated-4"], 128, 32, residue_stride=4,
+                                    return_lse=True, check=True)
     _check_sampled(o, lse, q, k, v, "dilated-4", [0, 7, 15], _sample_rows(N))
 
 
