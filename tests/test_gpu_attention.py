@@ -157,6 +157,25 @@ def test_dead_rows_and_all_dead():
     assert (o == 0).all() and torch.isneginf(lse).all()
 
 
+@pytest.mark.parametrize("name", ["causal", "dilated-8", "window-512"])
+def test_running_max_growth(name):
+    """Scores that grow from one quarter of the keys to the next by about 16, 49
+    and 147 (log2 units): the online softmax has to move its reference max as the
+    max grows, including growth far beyond what exponentials taken against the old
+    reference can hold."""
+    N, D, BH = 1024, 128, 2
+    g = torch.Generator().manual_seed(11)
+    q = 1.0 + 0.1 * torch.randn(BH, N, D, generator=g)
+    beta = torch.tensor([0.0, 1.0, 3.0, 9.0]).repeat_interleave(N // 4)
+    k = torch.randn(BH, N, D, generator=g) + beta[None, :, None]
+    v = torch.randn(BH, N, D, generator=g)
+    q, k, v = (t.to(torch.bfloat16).cuda() for t in (q, k, v))
+    o_ref, lse_ref = _oracle(q, k, v, name, N)
+    for BQ, A in ((128, 128), (128, 32), (64, 64), (16, 16)):
+        o, lse = _run(q, k, v, name, N, BQ, A)
+        _assert_close(o, lse, o_ref, lse_ref)
+
+
 @pytest.mark.parametrize("N,BQ,A", [(384, 128, 32), (1040, 16, 16), (640, 64, 64),
                                     (1024, 256, 256), (1536, 512, 128), (768, 48, 16)])
 def test_ragged_and_large_tiles(N, BQ, A):
