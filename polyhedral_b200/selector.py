@@ -26,14 +26,15 @@ others: ``offsets_of``).  Every cost is then exact arithmetic on those runs:
 
 ``select`` returns the reference's answer (ties broken towards class A, then
 by candidate order); ``select_class_a`` restricts the choice to what the
-kernel executes and returns the residue stride to pass as ``residue_stride``.
+kernel executes and returns the residue stride to pass as ``residue_stride``;
+``prepare`` builds everything the forward needs for that choice on the GPU.
 """
 from math import gcd
 
 import numpy as np
 
 __all__ = ["CANDIDATES", "RaggedNotSupported", "offsets_of", "tile_cost", "costs",
-           "select", "select_class_a", "is_class_b", "stride_of"]
+           "select", "select_class_a", "is_class_b", "stride_of", "prepare", "ClassAPlan"]
 
 CANDIDATES = (["identity", "shear"]
               + [f"stridefold-{s}" for s in (2, 4, 8)]
@@ -247,3 +248,33 @@ def select_class_a(mask, N, BQ, A):
                                  and (N // stride_of(k)) % 128 == 0)}
     name = min(ok, key=_rank(ok))
     return name, stride_of(name)
+
+
+class ClassAPlan:
+    """What ``prepare`` chose and built for one mask: the candidate, the residue
+    stride (0 = identity basis), the device block index of the mask in that basis
+    and the attention work list.  ``run(q, k, v)`` takes and returns tensors in
+    original row order."""
+
+    def __init__(self, mask, N, BQ, A, name, stride, index, plan):
+        self.mask, self.N, self.BQ, self.A = mask, N, BQ, A
+        self.name, self.stride, self.index, self.plan = name, stride, index, plan
+
+    def run(self, q, k, v, scale=None, return_lse=True):
+        from . import attention
+        kind, p0, p1, p2 = self.mask.spec
+        return attention.block_sparse_attention(
+            q, k, v, None, None, None, kind, p0, p1, p2, self.BQ, self.A, scale=scale,
+            residue_stride=self.stride, plan=self.plan, return_lse=return_lse)
+
+
+def prepare(mask, N, BQ, A, device="cuda"):
+    """Choose the executable basis with ``select_class_a`` and build, on the GPU,
+    the block index of the mask in that basis and the forward's work list."""
+    from . import attention, blockindex, permute
+    name, stride = select_class_a(mask, N, BQ, A)
+    perm = permute.residue_perm_device(N, stride, device) if stride else None
+    index = blockindex.build_device(mask, N, BQ, A, perm_q=perm, perm_kv=perm, device=device)
+    plan = attention.make_plan(index.kv_idx, index.kv_num, index.kv_partial, N, BQ, A,
+                               residue_stride=stride)
+    return ClassAPlan(mask, N, BQ, A, name, stride, index, plan)

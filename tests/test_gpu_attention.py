@@ -276,3 +276,18 @@ def test_config5_split_merge_full_size():
     o, lse = sp.run(q, k, v)
     torch.cuda.synchronize()
     _check_sampled(o, lse, q, k, v, "local1024+str16", [0, 127], _sample_rows(N, 48))
+
+
+@pytest.mark.parametrize("name,N,want", [("dilated-8", 2048, 8), ("local64+str8", 2048, 2),
+                                         ("window-128", 1024, 0), ("sinks4+win256", 1024, 0)])
+def test_selector_prepare_end_to_end(name, N, want):
+    """The selector's executable choice, built and run on the GPU, against the
+    oracle on the original mask (inputs and outputs in original order)."""
+    from polyhedral_b200 import masks, selector
+    m = masks.from_spec(*SPECS[name])
+    cp = selector.prepare(m, N, 128, 32)
+    assert cp.stride == want
+    q, k, v = _rand(2, N, 128, torch.bfloat16, seed=N + want)
+    o, lse = cp.run(q, k, v)
+    o_ref, lse_ref = _oracle(q, k, v, name, N)
+    _assert_close(o, lse, o_ref, lse_ref)
