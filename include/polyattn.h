@@ -68,7 +68,7 @@ typedef struct pa_pred {
 
 /* Message of the last failed call on this host thread ("" if none). */
 PA_API const char* pa_last_error(void);
-/* ABI revision of this header (2); bumped on any incompatible change. */
+/* ABI revision of this header (3); bumped on any incompatible change. */
 PA_API int pa_abi_version(void);
 
 /* ------------------------------------------------------------ block index
@@ -160,6 +160,13 @@ typedef struct pa_attn_args {
                                         o_row_map must be NULL and N/s must be a multiple of
                                         128 and of A.  The block index is that of the
                                         permuted mask, as with physically permuted inputs. */
+  int32_t merge;                     /* 0: write O and LSE.  1: O and LSE already hold the
+                                        result of an attention over a mask disjoint from this
+                                        one, on the same rows; the epilogue merges this one's
+                                        result into them (log-sum-exp merge, as pa_lse_merge)
+                                        instead of overwriting.  Needs lse != NULL.  No
+                                        counterpart in the reference, which never executes
+                                        the merge (src/polyattn/experiments/compose.py:7-17). */
 } pa_attn_args;
 
 /* Bytes of device workspace pa_attn_plan / pa_attn_fwd need for these arguments

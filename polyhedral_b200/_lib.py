@@ -38,7 +38,8 @@ class PaAttnArgs(ctypes.Structure):
                 ("kv_idx", c_vp), ("kv_num", c_vp), ("kv_partial", c_vp),
                 ("kv_stride", c_i32), ("BQ", c_i32), ("A", c_i32),
                 ("perm_q", c_vp), ("perm_kv", c_vp), ("o_row_map", c_vp),
-                ("pred", PaPred), ("scale", c_f32), ("residue_stride", c_i32)]
+                ("pred", PaPred), ("scale", c_f32), ("residue_stride", c_i32),
+                ("merge", c_i32)]
 
 
 class PaMergeArgs(ctypes.Structure):
@@ -72,7 +73,7 @@ SIGNATURES = {
     "pa_lse_merge": (ctypes.c_int, [ctypes.POINTER(PaMergeArgs), c_vp]),
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _lib = None
 

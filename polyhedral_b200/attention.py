@@ -16,7 +16,10 @@ the inverse permutation); ``plan`` reuses a work list built once by ``make_plan`
 the kernel reported a device-side failure; ``residue_stride=s`` takes q, k, v (and
 returns o, lse) in ORIGINAL row order and runs on their residue permutation by s
 without copying them (the kernel's tensor maps read row p of the permuted order
-directly; the block index is still that of the permuted mask).  The reference's class-B emulation
+directly; the block index is still that of the permuted mask); ``merge=True`` (with
+``out`` and ``lse_out``) treats them as holding the result of an attention over a
+disjoint mask on the same rows and merges this one into them in the epilogue
+(log-sum-exp merge, as ``merge.lse_merge``), so a split runs without a merge pass.  The reference's class-B emulation
 knobs (``gather_kv``, ``gather_mult``, ``gather_scatter``) are rejected when set;
 ``num_warps`` / ``num_stages`` are accepted and ignored.
 """
@@ -111,7 +114,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
                            gather_mult=1, gather_scatter=True,
                            num_warps=4, num_stages=2, *, return_lse=False,
                            o_row_map=None, plan=None, out=None, lse_out=None,
-                           check=False, residue_stride=0):
+                           check=False, residue_stride=0, merge=False):
     """q, k, v: [BH, N, D] (bf16 or fp16, D in {64, 128}), on one CUDA device.
     Returns o [BH, N, D] (same dtype), or (o, lse) with ``return_lse``."""
     if gather_kv or gather_mult != 1:
@@ -150,9 +153,11 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
                 and not torch.equal(plan.perm_kv, pk)):
             raise ValueError("plan was built for a different perm_kv")
 
+    if merge and (out is None or lse_out is None):
+        raise ValueError("merge=True merges into out / lse_out: pass both")
     o = out if out is not None else torch.empty((BH, N, D), dtype=q.dtype, device=dev)
     lse = None
-    if return_lse:
+    if return_lse or merge:
         lse = lse_out if lse_out is not None else torch.empty((BH, N), dtype=torch.float32,
                                                               device=dev)
 
@@ -174,6 +179,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     a.pred = _lib.PaPred(int(kind), int(p0), int(p1), int(p2))
     a.scale = float(scale) if scale else 0.0
     a.residue_stride = residue_stride
+    a.merge = 1 if merge else 0
     ws = plan.workspace
     _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
               _lib.stream_handle(dev))

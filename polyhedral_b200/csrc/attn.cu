@@ -251,6 +251,8 @@ int check_args(const pa_attn_args* a, const char* who) {
                "%s: A=%d unsupported (16, 32, 64, 128 or a multiple of 128)", who, a->A);
   PA_CHECK_ARG(a->N / a->A <= 65536 / 4, "%s: N/A=%d too many tiles per row", who,
                a->N / a->A);
+  PA_CHECK_ARG(a->merge == 0 || a->merge == 1, "%s: merge=%d must be 0 or 1", who, a->merge);
+  PA_CHECK_ARG(!a->merge || a->lse, "%s: merge needs the LSE of the result in place (lse)", who);
   if (a->residue_stride != 0) {
     const int rs = a->residue_stride;
     PA_CHECK_ARG(rs >= 1 && a->N % rs == 0, "%s: residue_stride=%d must divide N=%d", who, rs,
@@ -313,11 +315,15 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   const bool bf16 = a->dtype == PA_BF16;
   int rc2;
   if (a->D == 128)
-    rc2 = rs > 0 ? launch_d128_residue(tq, tk, tv, P, grid, L, bf16, stream)
-                 : launch_d128(tq, tk, tv, P, grid, L, bf16, stream);
+    rc2 = a->merge ? (rs > 0 ? launch_d128_residue_merge(tq, tk, tv, P, grid, L, bf16, stream)
+                             : launch_d128_merge(tq, tk, tv, P, grid, L, bf16, stream))
+                   : (rs > 0 ? launch_d128_residue(tq, tk, tv, P, grid, L, bf16, stream)
+                             : launch_d128(tq, tk, tv, P, grid, L, bf16, stream));
   else
-    rc2 = rs > 0 ? launch_d64_residue(tq, tk, tv, P, grid, L, bf16, stream)
-                 : launch_d64(tq, tk, tv, P, grid, L, bf16, stream);
+    rc2 = a->merge ? (rs > 0 ? launch_d64_residue_merge(tq, tk, tv, P, grid, L, bf16, stream)
+                             : launch_d64_merge(tq, tk, tv, P, grid, L, bf16, stream))
+                   : (rs > 0 ? launch_d64_residue(tq, tk, tv, P, grid, L, bf16, stream)
+                             : launch_d64(tq, tk, tv, P, grid, L, bf16, stream));
   if (rc2) return rc2;
   return check_launch("pa_attn_fwd");
 }

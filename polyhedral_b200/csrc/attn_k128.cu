@@ -6,7 +6,7 @@ namespace attn {
 
 int launch_d128(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P, int grid, int L,
        bool bf16, cudaStream_t stream) {
-  return launch_family<128, false>(tq, tk, tv, P, grid, L, bf16, stream);
+  return launch_family<128, false, false>(tq, tk, tv, P, grid, L, bf16, stream);
 }
 
 }  // namespace attn

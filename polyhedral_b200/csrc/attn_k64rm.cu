@@ -1,0 +1,13 @@
+// Instantiations of the attention forward kernel for D = 64, inputs read through a residue permutation, merging into the O / LSE in place.
+#include "attn_kernel.cuh"
+
+namespace pa {
+namespace attn {
+
+int launch_d64_residue_merge(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P, int grid, int L,
+       bool bf16, cudaStream_t stream) {
+  return launch_family<64, true, true>(tq, tk, tv, P, grid, L, bf16, stream);
+}
+
+}  // namespace attn
+}  // namespace pa

@@ -107,6 +107,18 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 template <bool kBf16>
+__device__ __forceinline__ void unpack2(uint32_t u, float& lo, float& hi) {
+  if constexpr (kBf16) {
+    lo = __uint_as_float(u << 16);
+    hi = __uint_as_float(u & 0xffff0000u);
+  } else {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
+    lo = f.x;
+    hi = f.y;
+  }
+}
+
+template <bool kBf16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (kBf16) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -253,7 +265,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-template <int D, int L, bool kBf16, bool kRS>
+template <int D, int L, bool kBf16, bool kRS, bool kMerge>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const FwdParams P) {
@@ -546,6 +558,25 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
                        : kRS          ? (row % P.nb) * P.rs + row / P.nb
                        : P.perm_q    ? __ldg(P.perm_q + row)
                                      : row;
+      // merge: the LSE in place is read now and the O row in place is pulled into
+      // L2, so the epilogue does not wait on memory for them
+      float lse_prev = -INFINITY;
+      if constexpr (kMerge) {
+        if (valid) {
+          const int orw0 = kRS          ? (row % P.nb) * P.rs + row / P.nb
+                           : P.o_row_map ? __ldg(P.o_row_map + row)
+                                         : row;
+          if ((unsigned)orw0 < (unsigned)P.N) {
+            const char* op = static_cast<const char*>(P.o) +
+                             ((long long)bh * P.o_bh_stride + (long long)orw0 * P.o_row_stride) * 2;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(op));
+            if constexpr (D == 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(op + 128));
+            asm volatile("ld.global.f32 %0, [%1];"
+                         : "=f"(lse_prev)
+                         : "l"(P.lse + (long long)bh * P.lse_bh_stride + orw0));
+          }
+        }
+      }
       float m_used = -INFINITY, l = 0.f;
       bool ok = true;
       for (int u = 0; u < nsup; ++u) {
@@ -712,6 +743,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       // epilogue: O / l, LSE
       float inv_l = l > 0.f ? 1.f / l : 0.f;
       const float lse_v = l > 0.f ? (m_used + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+      float w_old = 0.f;   // weight of the O row already in place (merge)
       char* orow = nullptr;
       if (valid) {
         const int orw = kRS          ? (row % P.nb) * P.rs + row / P.nb
@@ -720,12 +752,33 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         if ((unsigned)orw < (unsigned)P.N) {
           orow = static_cast<char*>(P.o) +
                  ((long long)bh * P.o_bh_stride + (long long)orw * P.o_row_stride) * 2;
-          if (P.lse) P.lse[(long long)bh * P.lse_bh_stride + orw] = lse_v;
+          if (P.lse) {
+            float* lp = P.lse + (long long)bh * P.lse_bh_stride + orw;
+            if constexpr (kMerge) {
+              // The row already holds the result (O1, l1) of a disjoint part:
+              // O = (e^(l1-m) O1 + e^(l2-m) O2) / (e^(l1-m) + e^(l2-m)), m = max(l1, l2),
+              // LSE = m + log(e^(l1-m) + e^(l2-m)); this part's weight folds into 1/l.
+              const float lo = lse_prev;
+              const float mm = fmaxf(lo, lse_v);
+              float wa = 0.f, wb = 0.f;
+              if (mm != -INFINITY) {
+                wa = expf(lo - mm);
+                wb = expf(lse_v - mm);
+              }
+              const float den = wa + wb;
+              const float inv = den > 0.f ? 1.f / den : 0.f;
+              w_old = wa * inv;
+              inv_l *= wb * inv;
+              *lp = den > 0.f ? mm + logf(den) : -INFINITY;
+            } else {
+              *lp = lse_v;
+            }
+          }
         }
       }
       // O leaves through a per-warp staging buffer so that every global store
       // writes whole 128-byte row segments (8 lanes per row), including when rows
-      // are scattered by o_row_map.
+      // are scattered by o_row_map; a merge reads the rows in place the same way.
       uint8_t* stage = sEpi + warp * (32 * 128);
       const bool have_o = nsup > 0;
       if (have_o) {
@@ -734,41 +787,110 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         if (!__all_sync(0xffffffffu, ok)) break;
         tc_fence_after();
       }
+      if constexpr (!kMerge) {
 #pragma unroll
-      for (int dh = 0; dh < D / 64; ++dh) {
-        uint32_t w[32];   // 64 outputs of this row, packed in pairs
-        if (have_o) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32(tO + dh * 64, r0);
-          tmem_ld32(tO + dh * 64 + 32, r1);
-          tmem_wait_ld();
-          tmem_regs_ready(r0);
-          tmem_regs_ready(r1);
+        for (int dh = 0; dh < D / 64; ++dh) {
+          uint32_t w[32];   // 64 outputs of this row, packed in pairs
+          if (have_o) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tO + dh * 64, r0);
+            tmem_ld32(tO + dh * 64 + 32, r1);
+            tmem_wait_ld();
+            tmem_regs_ready(r0);
+            tmem_regs_ready(r1);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            w[i] = pack2<kBf16>(__uint_as_float(r0[2 * i]) * inv_l,
-                                __uint_as_float(r0[2 * i + 1]) * inv_l);
-            w[16 + i] = pack2<kBf16>(__uint_as_float(r1[2 * i]) * inv_l,
-                                     __uint_as_float(r1[2 * i + 1]) * inv_l);
+            for (int i = 0; i < 16; ++i) {
+              w[i] = pack2<kBf16>(__uint_as_float(r0[2 * i]) * inv_l,
+                                  __uint_as_float(r0[2 * i + 1]) * inv_l);
+              w[16 + i] = pack2<kBf16>(__uint_as_float(r1[2 * i]) * inv_l,
+                                       __uint_as_float(r1[2 * i + 1]) * inv_l);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) w[i] = 0u;
           }
-        } else {
+          __syncwarp();   // the previous round's readers are done with the buffer
 #pragma unroll
-          for (int i = 0; i < 32; ++i) w[i] = 0u;
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+          __syncwarp();
+          const int c = lane & 7;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+            const unsigned long long dst =
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
+            if (dst) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + dh * 128 + c * 16) = v;
+          }
         }
-        __syncwarp();   // the previous round's readers are done with the buffer
+      } else {
+        // merge: the rows in place are read through the staging buffer the same way
+        const int cc = lane & 7;
+#pragma unroll 1
+        for (int dh = 0; dh < D / 64; ++dh) {
+          // all eight loads are issued before the first shared-memory store, so the
+          // round trips to memory overlap
+          uint4 ov[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
-              make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-        __syncwarp();
-        const int c = lane & 7;
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            const unsigned long long src =
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
+            ov[it] = make_uint4(0u, 0u, 0u, 0u);
+            if (src)
+              asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(ov[it].x), "=r"(ov[it].y), "=r"(ov[it].z), "=r"(ov[it].w)
+                           : "l"(reinterpret_cast<const char*>(src) + dh * 128 + cc * 16));
+          }
+          __syncwarp();   // the previous round's readers are done with the buffer
 #pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int rr = it * 4 + (lane >> 3);
-          const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
-          const unsigned long long dst =
-              __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
-          if (dst) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + dh * 128 + c * 16) = v;
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            *reinterpret_cast<uint4*>(stage + rr * 128 + ((cc ^ (rr & 7)) << 4)) = ov[it];
+          }
+          __syncwarp();
+          uint32_t w[32];
+#pragma unroll
+          for (int half32 = 0; half32 < 2; ++half32) {
+            uint32_t r[32];
+            if (have_o) {
+              tmem_ld32(tO + dh * 64 + half32 * 32, r);
+              tmem_wait_ld();
+              tmem_regs_ready(r);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = 0u;
+            }
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4) {
+              const int c = half32 * 4 + c4;
+              const uint4 v = *reinterpret_cast<const uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4));
+              const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float a, b2;
+                unpack2<kBf16>(vv[j], a, b2);
+                w[4 * c + j] = pack2<kBf16>(fmaf(w_old, a, __uint_as_float(r[8 * c4 + 2 * j]) * inv_l),
+                                            fmaf(w_old, b2, __uint_as_float(r[8 * c4 + 2 * j + 1]) * inv_l));
+              }
+            }
+          }
+          __syncwarp();   // every lane has read its old row
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + (lane >> 3);
+            const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((cc ^ (rr & 7)) << 4));
+            const unsigned long long dst =
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
+            if (dst) *reinterpret_cast<uint4*>(reinterpret_cast<char*>(dst) + dh * 128 + cc * 16) = v;
+          }
         }
       }
       if (have_o) tc_fence_before();
@@ -802,10 +924,14 @@ PA_DECLARE_LAUNCH(launch_d128)
 PA_DECLARE_LAUNCH(launch_d128_residue)
 PA_DECLARE_LAUNCH(launch_d64)
 PA_DECLARE_LAUNCH(launch_d64_residue)
+PA_DECLARE_LAUNCH(launch_d128_merge)
+PA_DECLARE_LAUNCH(launch_d128_residue_merge)
+PA_DECLARE_LAUNCH(launch_d64_merge)
+PA_DECLARE_LAUNCH(launch_d64_residue_merge)
 #undef PA_DECLARE_LAUNCH
 
 // Body of the launchers: pick the instantiation for (L, dtype).
-template <int D, bool kRS>
+template <int D, bool kRS, bool kMerge>
 int launch_family(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P, int grid,
                   int L, bool bf16, cudaStream_t stream) {
   auto go = [&](auto kernel) -> int {
@@ -816,10 +942,14 @@ int launch_family(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParam
     return PA_OK;
   };
   switch (L) {
-    case 16: return bf16 ? go(attn_fwd_kernel<D, 16, true, kRS>) : go(attn_fwd_kernel<D, 16, false, kRS>);
-    case 32: return bf16 ? go(attn_fwd_kernel<D, 32, true, kRS>) : go(attn_fwd_kernel<D, 32, false, kRS>);
-    case 64: return bf16 ? go(attn_fwd_kernel<D, 64, true, kRS>) : go(attn_fwd_kernel<D, 64, false, kRS>);
-    default: return bf16 ? go(attn_fwd_kernel<D, 128, true, kRS>) : go(attn_fwd_kernel<D, 128, false, kRS>);
+    case 16: return bf16 ? go(attn_fwd_kernel<D, 16, true, kRS, kMerge>)
+                         : go(attn_fwd_kernel<D, 16, false, kRS, kMerge>);
+    case 32: return bf16 ? go(attn_fwd_kernel<D, 32, true, kRS, kMerge>)
+                         : go(attn_fwd_kernel<D, 32, false, kRS, kMerge>);
+    case 64: return bf16 ? go(attn_fwd_kernel<D, 64, true, kRS, kMerge>)
+                         : go(attn_fwd_kernel<D, 64, false, kRS, kMerge>);
+    default: return bf16 ? go(attn_fwd_kernel<D, 128, true, kRS, kMerge>)
+                         : go(attn_fwd_kernel<D, 128, false, kRS, kMerge>);
   }
 }
 

@@ -11,7 +11,9 @@ two parts would be counted twice in the softmax denominator.
 A part in a residue-permuted basis runs on Q/K/V in their original row order: the
 kernel reads the permuted order through strided tensor maps (``residue_stride``),
 evaluates the predicate in original coordinates and writes O/LSE back in original
-order, so no part copies Q/K/V and the merge needs no row map.
+order, so no part copies Q/K/V.  Every part after the first merges its result into
+the O/LSE already written (the attention epilogue's ``merge``), so the split costs no
+separate merge pass over O.
 """
 from dataclasses import dataclass
 from typing import Optional
@@ -19,7 +21,7 @@ from typing import Optional
 import numpy as np
 import torch
 
-from . import attention, blockindex, masks, merge, permute
+from . import attention, blockindex, masks, permute
 
 
 @dataclass
@@ -51,19 +53,20 @@ class SplitPlan:
             self.indices.append(dbi)
             self.plans.append(plan)
 
-    def run(self, q, k, v, scale=None, out=None):
-        """(o, lse) of the union mask, rows in original order."""
-        o = lse = None
+    def run(self, q, k, v, scale=None, out=None, lse_out=None):
+        """(o, lse) of the union mask, rows in original order.  The first part
+        writes O / LSE; each later part merges its result into them in its own
+        epilogue (``merge=True``), so no separate merge pass runs."""
+        BH, N, D = q.shape
+        o = out if out is not None else torch.empty_like(q)
+        lse = lse_out if lse_out is not None else torch.empty((BH, N), dtype=torch.float32,
+                                                              device=q.device)
         for i, part in enumerate(self.parts):
             kind, p0, p1, p2 = part.mask.spec
-            oi, li = attention.block_sparse_attention(
+            attention.block_sparse_attention(
                 q, k, v, None, None, None, kind, p0, p1, p2, part.BQ, part.A,
                 scale=scale, residue_stride=part.stride, plan=self.plans[i], return_lse=True,
-                out=(out if (i == 0 and out is not None) else None))
-            if o is None:
-                o, lse = oi, li
-            else:
-                o, lse = merge.lse_merge(o, lse, oi, li, out=o, lse_out=lse)
+                out=o, lse_out=lse, merge=i > 0)
         return o, lse
 
     def live_count(self):

@@ -58,3 +58,72 @@ def test_split_equals_union_attention():
         o_ref, lse_ref = O.attention_heads(q.float().cpu(), k.float().cpu(), v.float().cpu(), M)
         assert (o.float().cpu() - o_ref).abs().max().item() < 2e-2
         assert (lse.cpu() - lse_ref).abs().max().item() < 2e-2
+
+
+def _union_ref(q, k, v, M):
+    return O.attention_heads(q.float().cpu(), k.float().cpu(), v.float().cpu(),
+                             torch.from_numpy(M))
+
+
+def _part(q, k, v, mask, N, BQ, A, stride=0, **kw):
+    from polyhedral_b200 import attention, blockindex, permute
+    perm = permute.residue_perm_device(N, stride, q.device) if stride else None
+    dbi = blockindex.build_device(mask, N, BQ, A, perm_q=perm, perm_kv=perm, device=q.device)
+    kind, p0, p1, p2 = mask.spec
+    return attention.block_sparse_attention(q, k, v, dbi.kv_idx, dbi.kv_num, dbi.kv_partial,
+                                            kind, p0, p1, p2, BQ, A, residue_stride=stride,
+                                            return_lse=True, check=True, **kw)
+
+
+@pytest.mark.parametrize("stride2", [0, 8])
+@pytest.mark.parametrize("BQ,A", [(128, 32), (128, 128), (64, 64), (16, 16)])
+def test_fused_merge_matches_union(stride2, BQ, A):
+    """Part 2 merged into part 1 by the attention epilogue equals attention over
+    the union mask; rows dead in part 1 (far band) and rows dead in both."""
+    from polyhedral_b200 import masks
+    N, D, BH = 2048, 128, 2
+    g = torch.Generator().manual_seed(21)
+    q, k, v = (torch.randn(BH, N, D, generator=g).bfloat16().cuda() for _ in range(3))
+    p1, p2 = masks.FarStrided(1024, 8), masks.SlidingWindow(256)
+    if stride2:   # part 2 in a residue basis: the far lattice band
+        p1, p2 = masks.SlidingWindow(256), masks.FarStrided(1024, 8)
+    o, lse = _part(q, k, v, p1, N, BQ, A)
+    _part(q, k, v, p2, N, BQ, A, stride2, out=o, lse_out=lse, merge=True)
+    M = p1.dense(N) | p2.dense(N)
+    o_ref, lse_ref = _union_ref(q, k, v, M)
+    assert (o.float().cpu() - o_ref).abs().max().item() < 2e-2
+    fin = torch.isfinite(lse_ref)
+    assert torch.equal(torch.isfinite(lse.cpu()), fin)
+    assert (lse.cpu()[fin] - lse_ref[fin]).abs().max().item() < 2e-2
+    # both parts dead: rows where neither mask has a live key stay O = 0, LSE = -inf
+    q2 = q[:, :512].contiguous()
+    k2, v2 = k[:, :512].contiguous(), v[:, :512].contiguous()
+    far, far2 = masks.FarStrided(600, 8), masks.FarStrided(700, 4)
+    o, lse = _part(q2, k2, v2, far, 512, 128, 32)
+    _part(q2, k2, v2, far2, 512, 128, 32, out=o, lse_out=lse, merge=True)
+    assert (o == 0).all() and torch.isneginf(lse).all()
+
+
+def test_fused_merge_equals_merge_kernel():
+    """The fused merge and attention + pa_lse_merge agree within one bf16 rounding
+    (the fused path merges this part's fp32 result before rounding)."""
+    from polyhedral_b200 import masks, merge
+    N, D, BH = 1024, 64, 3
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn(BH, N, D, generator=g).bfloat16().cuda() for _ in range(3))
+    a, b = masks.SlidingWindow(100), masks.FarStrided(100, 4)
+    o1, l1 = _part(q, k, v, a, N, 128, 32)
+    o2, l2 = _part(q, k, v, b, N, 128, 32)
+    ref_o, ref_l = merge.lse_merge(o1, l1, o2, l2)
+    o, lse = o1.clone(), l1.clone()
+    _part(q, k, v, b, N, 128, 32, out=o, lse_out=lse, merge=True)
+    assert (o.float() - ref_o.float()).abs().max().item() < 1.6e-2
+    assert (lse - ref_l).abs().max().item() < 1e-5
+
+
+def test_fused_merge_argument_errors():
+    from polyhedral_b200 import _lib, masks
+    N = 512
+    q, k, v = (torch.zeros(1, N, 128, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    with pytest.raises(ValueError):
+        _part(q, k, v, masks.Causal(), N, 128, 32, merge=True)
