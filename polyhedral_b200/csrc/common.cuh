@@ -63,29 +63,18 @@ PA_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
-// As mbar_try_wait, but the thread may sleep in hardware for up to `hint_ns`
-// nanoseconds while the phase is incomplete (it wakes as soon as it completes),
-// so a waiting warp does not take issue slots from the warps doing work.
-PA_DEV bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns) : "memory");
-  return ok != 0;
-}
-
 // Wait for the phase of `bar` with parity `parity` to complete.  Gives up after
 // kWaitLimitNs, or as soon as another thread of the CTA has raised `*abort`;
 // on its own timeout it raises `*abort` and records `code` in `*err` (global).
-// Returns false when it gave up.
+// Returns false when it gave up.  try_wait itself blocks in hardware for a
+// system-defined time before returning false; a suspend-time hint (measured)
+// made the attention kernel about 1.5 % slower, so none is given.
 PA_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                       int32_t* err, int32_t code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > kWaitLimitNs) {
       *abort = 1;
