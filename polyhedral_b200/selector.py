@@ -34,7 +34,8 @@ from math import gcd
 import numpy as np
 
 __all__ = ["CANDIDATES", "RaggedNotSupported", "offsets_of", "tile_cost", "costs",
-           "select", "select_class_a", "is_class_b", "stride_of", "prepare", "ClassAPlan"]
+           "select", "select_class_a", "is_class_b", "stride_of", "prepare", "ClassAPlan",
+           "costs_device"]
 
 CANDIDATES = (["identity", "shear"]
               + [f"stridefold-{s}" for s in (2, 4, 8)]
@@ -248,6 +249,30 @@ def select_class_a(mask, N, BQ, A):
                                  and (N // stride_of(k)) % 128 == 0)}
     name = min(ok, key=_rank(ok))
     return name, stride_of(name)
+
+
+def costs_device(mask, N, BQ, A, device="cuda"):
+    """{candidate: elements computed} for identity and every residue-perm-s with
+    N/s a multiple of BQ and A, measured by building each candidate's block index
+    on the GPU (``blockindex.build_device``, the tiles it lists times BQ*A).  Works
+    for masks that are not diagonally invariant as well, where the closed forms of
+    ``costs`` do not apply; on invariant masks it equals ``costs`` exactly."""
+    import torch
+    from . import blockindex, permute
+    out, stats = {}, []
+    for name in CANDIDATES:
+        if is_class_b(name):
+            continue
+        s = stride_of(name)
+        if s and (N % s or (N // s) % BQ or (N // s) % A):
+            continue
+        perm = permute.residue_perm_device(N, s, device) if s else None
+        dbi = blockindex.build_device(mask, N, BQ, A, perm_q=perm, perm_kv=perm, device=device)
+        stats.append((name, dbi.stats))
+    torch.cuda.synchronize(device)
+    for name, st in stats:
+        out[name] = int(st[0].item())
+    return out
 
 
 class ClassAPlan:

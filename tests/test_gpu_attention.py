@@ -291,3 +291,21 @@ def test_selector_prepare_end_to_end(name, N, want):
     o, lse = cp.run(q, k, v)
     o_ref, lse_ref = _oracle(q, k, v, name, N)
     _assert_close(o, lse, o_ref, lse_ref)
+
+
+@pytest.mark.parametrize("name,N", [("dilated-4", 8192), ("local64+str8", 16384),
+                                    ("window-128", 1024), ("local256+str8", 4096)])
+def test_selector_device_costs_equal_closed_form(name, N):
+    """Class-A costs measured by building each candidate's block index on the GPU
+    equal the selector's closed forms, integer for integer."""
+    from polyhedral_b200 import masks, selector
+    m = masks.from_spec(*SPECS[name])
+    for BQ, A in ((128, 32), (128, 128), (16, 16)):
+        dev = selector.costs_device(m, N, BQ, A)
+        host = {k: v for k, v in selector.costs(m, N, BQ, A).items()
+                if not selector.is_class_b(k)}
+        assert dev == host, (BQ, A)
+    # a mask that is not diagonally invariant still gets device costs
+    sk = masks.SinksWindow(4, 512)
+    assert selector.costs(sk, 8192, 128, 32) is None
+    assert selector.costs_device(sk, 8192, 128, 32)["identity"] == 5320704
