@@ -43,13 +43,16 @@ WORKLOADS = {
     "c2": (1, 16, 8192, 128, "dilated-4", 4, 128, 32, 1,
            "c2: dilated-4 + residue-perm-4, 128x32 tiles, B1 H16 N8192 D128 bf16"),
     "c3": (2, 16, 16384, 128, "local64+str8", 8, 128, 32, 2,
-           "c3: local64+str8 + residue-perm-8, 128x32 tiles, B2 H16 N16384 D128 bf16"),
+           "c3: local64+str8 + residue-perm-8, 128x32 tiles, 64-row KV super-tiles, B2 H16 N16384 D128 bf16"),
     "c4": (4, 32, 8192, 128, "sinks4+win512", 0, 128, 32, 3,
-           "c4: sinks4+win512, 128x32 tiles, B4 H32 N8192 D128 bf16"),
+           "c4: sinks4+win512, 128x32 tiles, 64-row KV super-tiles, B4 H32 N8192 D128 bf16"),
     "c5": (2, 64, 32768, 128, "local1024+str16", 16, 128, 64, 4,
            "c5: window-1024 (identity, 128x128) + far1024+str16 (residue-perm-16, 128x64) "
            "split, LSE merge fused into the second part's epilogue, B2 H64 N32768 D128 bf16"),
 }
+# KV rows per super-tile of the attention kernel, per workload (default 128); the
+# 64-row kernel wins where many tiles are partial (lattice and sinks masks)
+KV_ROWS = {"c3": 64, "c4": 64}
 
 
 def _peaks():
@@ -161,6 +164,8 @@ class Pipeline:
         import torch
         from polyhedral_b200 import attention, blockindex, masks_gpu, permute, split
         B, H, N, D, name, s, BQ, A, seed, _ = WORKLOADS[wl]
+        # mask-heavy workloads (many partial tiles) run the 64-row super-tile kernel
+        self.kv_rows = KV_ROWS.get(wl, 0)
         self.wl, self.B, self.H, self.N, self.D = wl, B, H, N, D
         self.name, self.s, self.BQ, self.A = name, s, BQ, A
         self.device = device
@@ -195,7 +200,7 @@ class Pipeline:
             return self.split.run(q, k, v, out=o, lse_out=lse)
         return attention.block_sparse_attention(
             q, k, v, None, None, None, *self.spec, self.BQ, self.A, residue_stride=self.s,
-            plan=self.plan, return_lse=True, out=o, lse_out=lse)
+            plan=self.plan, return_lse=True, out=o, lse_out=lse, kv_rows=self.kv_rows)
 
     attn_only = step
 

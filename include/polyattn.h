@@ -68,7 +68,7 @@ typedef struct pa_pred {
 
 /* Message of the last failed call on this host thread ("" if none). */
 PA_API const char* pa_last_error(void);
-/* ABI revision of this header (3); bumped on any incompatible change. */
+/* ABI revision of this header (4); bumped on any incompatible change. */
 PA_API int pa_abi_version(void);
 
 /* ------------------------------------------------------------ block index
@@ -167,6 +167,11 @@ typedef struct pa_attn_args {
                                         instead of overwriting.  Needs lse != NULL.  No
                                         counterpart in the reference, which never executes
                                         the merge (src/polyattn/experiments/compose.py:7-17). */
+  int32_t kv_rows;                   /* KV rows per super-tile of the forward: 0 or 128 (the
+                                        default kernel), or 64 (S double-buffered in TMEM so
+                                        the next S runs during the softmax; faster where many
+                                        tiles are partial, e.g. lattice and sinks masks).  64
+                                        cannot be combined with merge. */
 } pa_attn_args;
 
 /* Bytes of device workspace pa_attn_plan / pa_attn_fwd need for these arguments

@@ -39,7 +39,7 @@ class PaAttnArgs(ctypes.Structure):
                 ("kv_stride", c_i32), ("BQ", c_i32), ("A", c_i32),
                 ("perm_q", c_vp), ("perm_kv", c_vp), ("o_row_map", c_vp),
                 ("pred", PaPred), ("scale", c_f32), ("residue_stride", c_i32),
-                ("merge", c_i32)]
+                ("merge", c_i32), ("kv_rows", c_i32)]
 
 
 class PaMergeArgs(ctypes.Structure):
@@ -73,7 +73,7 @@ SIGNATURES = {
     "pa_lse_merge": (ctypes.c_int, [ctypes.POINTER(PaMergeArgs), c_vp]),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _lib = None
 

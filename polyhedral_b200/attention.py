@@ -19,7 +19,10 @@ without copying them (the kernel's tensor maps read row p of the permuted order
 directly; the block index is still that of the permuted mask); ``merge=True`` (with
 ``out`` and ``lse_out``) treats them as holding the result of an attention over a
 disjoint mask on the same rows and merges this one into them in the epilogue
-(log-sum-exp merge, as ``merge.lse_merge``), so a split runs without a merge pass.  The reference's class-B emulation
+(log-sum-exp merge, as ``merge.lse_merge``), so a split runs without a merge pass;
+``kv_rows=64`` selects the 64-row super-tile kernel (S double-buffered in TMEM:
+faster where many tiles are partial, slower on mostly full tiles; not with
+``merge``).  The reference's class-B emulation
 knobs (``gather_kv``, ``gather_mult``, ``gather_scatter``) are rejected when set;
 ``num_warps`` / ``num_stages`` are accepted and ignored.
 """
@@ -114,7 +117,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
                            gather_mult=1, gather_scatter=True,
                            num_warps=4, num_stages=2, *, return_lse=False,
                            o_row_map=None, plan=None, out=None, lse_out=None,
-                           check=False, residue_stride=0, merge=False):
+                           check=False, residue_stride=0, merge=False, kv_rows=0):
     """q, k, v: [BH, N, D] (bf16 or fp16, D in {64, 128}), on one CUDA device.
     Returns o [BH, N, D] (same dtype), or (o, lse) with ``return_lse``."""
     if gather_kv or gather_mult != 1:
@@ -180,6 +183,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     a.scale = float(scale) if scale else 0.0
     a.residue_stride = residue_stride
     a.merge = 1 if merge else 0
+    a.kv_rows = int(kv_rows or 0)
     ws = plan.workspace
     _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
               _lib.stream_handle(dev))

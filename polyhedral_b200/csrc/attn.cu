@@ -35,6 +35,7 @@
 #include <math.h>
 #include <mutex>
 #include "attn_kernel.cuh"
+#include "attn_kernel_db.cuh"
 
 namespace pa {
 namespace attn {
@@ -252,6 +253,10 @@ int check_args(const pa_attn_args* a, const char* who) {
   PA_CHECK_ARG(a->N / a->A <= 65536 / 4, "%s: N/A=%d too many tiles per row", who,
                a->N / a->A);
   PA_CHECK_ARG(a->merge == 0 || a->merge == 1, "%s: merge=%d must be 0 or 1", who, a->merge);
+  PA_CHECK_ARG(a->kv_rows == 0 || a->kv_rows == 128 || a->kv_rows == 64,
+               "%s: kv_rows=%d must be 0, 128 or 64", who, a->kv_rows);
+  if (a->kv_rows == 64 && a->merge)
+    return fail(PA_ERR_UNSUPPORTED, "%s: kv_rows=64 cannot be combined with merge", who);
   PA_CHECK_ARG(!a->merge || a->lse, "%s: merge needs the LSE of the result in place (lse)", who);
   if (a->residue_stride != 0) {
     const int rs = a->residue_stride;
@@ -268,7 +273,9 @@ int check_args(const pa_attn_args* a, const char* who) {
 
 int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   CUtensorMap tq, tk, tv;
-  const int L = a->A < BN ? a->A : BN;
+  const bool rows64 = a->kv_rows == 64;
+  const int bn = rows64 ? db::BN : BN;
+  const int L = a->A < bn ? a->A : bn;
   int rc;
   const int rs = a->residue_stride;
   if ((rc = make_tmap(&tq, a->q, a->dtype, a->BH, a->N, a->D, a->q_row_stride, a->q_bh_stride,
@@ -303,7 +310,7 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   P.scale_log2 = scale * 1.4426950408889634f;
   P.pv = pv;
   const uint32_t fmt = a->dtype == PA_BF16 ? 1u : 0u;
-  P.idesc_qk = make_idesc_f16(fmt, BM, BN, 0, 0);
+  P.idesc_qk = make_idesc_f16(fmt, BM, bn, 0, 0);
   P.idesc_pv = make_idesc_f16(fmt, BM, a->D, 0, 1);
   P.total_items = pv.npairs * a->BH;
 
@@ -314,7 +321,13 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
 
   const bool bf16 = a->dtype == PA_BF16;
   int rc2;
-  if (a->D == 128)
+  if (rows64 && a->D == 128)
+    rc2 = rs > 0 ? db::launch_d128_residue(tq, tk, tv, P, grid, L, bf16, stream)
+                 : db::launch_d128(tq, tk, tv, P, grid, L, bf16, stream);
+  else if (rows64)
+    rc2 = rs > 0 ? db::launch_d64_residue(tq, tk, tv, P, grid, L, bf16, stream)
+                 : db::launch_d64(tq, tk, tv, P, grid, L, bf16, stream);
+  else if (a->D == 128)
     rc2 = a->merge ? (rs > 0 ? launch_d128_residue_merge(tq, tk, tv, P, grid, L, bf16, stream)
                              : launch_d128_merge(tq, tk, tv, P, grid, L, bf16, stream))
                    : (rs > 0 ? launch_d128_residue(tq, tk, tv, P, grid, L, bf16, stream)
