@@ -127,3 +127,49 @@ def test_fused_merge_argument_errors():
     q, k, v = (torch.zeros(1, N, 128, dtype=torch.bfloat16, device="cuda") for _ in range(3))
     with pytest.raises(ValueError):
         _part(q, k, v, masks.Causal(), N, 128, 32, merge=True)
+
+
+def test_reference_style_driver_runs_on_the_dropin(tmp_path):
+    """A driver written the way the reference's gpu/exp*.py are (bare-name imports,
+    bench.time_ms / report, identity vs residue-permuted run) runs through
+    ``python -m polyhedral_b200.dropin`` and agrees with itself across the
+    permutation."""
+    import subprocess
+    import sys
+    import textwrap
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    script = tmp_path / "driver.py"
+    script.write_text(textwrap.dedent("""
+        import sys
+        sys.path.insert(0, __file__.rsplit("/", 1)[0])
+        import torch
+        import blockindex, bench, masks_gpu, permute
+        from triton_attn import block_sparse_attention
+        N, D, BH, name, s = 2048, 64, 4, "dilated-8", 8
+        g = torch.Generator().manual_seed(0)
+        q, k, v = (torch.randn(BH, N, D, generator=g).half().cuda() for _ in range(3))
+        m, spec = masks_gpu.numpy_mask(name), masks_gpu.triton_params(name)
+        rows = []
+        for BQ, A in ((128, 128), (16, 16)):
+            kvi, kvn, kvp = blockindex.to_cuda(blockindex.build(m, N, BQ, A))
+            f0 = lambda: block_sparse_attention(q, k, v, kvi, kvn, kvp, *spec, BQ, A,
+                                                num_warps=4, num_stages=2)
+            p = torch.from_numpy(permute.residue_perm(N, s)).cuda()
+            pk = blockindex.to_cuda(blockindex.build(m, N, BQ, A, perm_q=p, perm_kv=p))
+            qp, kp, vp = (permute.apply_perm(x, p) for x in (q, k, v))
+            f1 = lambda: block_sparse_attention(qp, kp, vp, *pk, *spec, BQ, A, perm_q=p)
+            o0 = f0()
+            o1 = f1().index_select(1, permute.invert(p).long())
+            err = (o0.float() - o1.float()).abs().max().item()
+            assert err < 1e-2, err
+            t0, _ = bench.time_ms(f0, warmup=3, reps=10)
+            t1, _ = bench.time_ms(f1, warmup=3, reps=10)
+            rows.append((f"{BQ}x{A}", t0, t1))
+        bench.report(rows, [("tile", 8), ("identity", 10), ("rp8", 10)], title="driver")
+        print("DRIVER OK")
+    """))
+    r = subprocess.run([sys.executable, "-m", "polyhedral_b200.dropin", str(script)], cwd=root,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "DRIVER OK" in r.stdout
