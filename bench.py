@@ -299,6 +299,30 @@ def run_ours(args, rank, world, device):
                      "peak_source": f"{hbm_kind} HBM copy"}
         del pouts
 
+    # the standalone LSE merge (pa_lse_merge), HBM-bound; the c5 step itself merges
+    # in the attention epilogue instead
+    merge_line = None
+    if pipe.split is not None:
+        from polyhedral_b200 import merge as merge_mod
+        o1, l1 = outs[0]
+        o2, l2 = outs[1]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(2):
+            merge_mod.lse_merge(o1, l1, o2, l2, out=o1, lse_out=l1)
+        e0.record()
+        mreps = max(3, min(reps, 20))
+        for i in range(mreps):
+            merge_mod.lse_merge(o1, l1, o2, l2, out=o1, lse_out=l1)
+        e1.record()
+        torch.cuda.synchronize(device)
+        mms = e0.elapsed_time(e1) / mreps
+        mbytes = 3 * (B * H * N * D * 2 + B * H * N * 4)
+        _, _, hbm_peak, hbm_kind = _peaks()
+        merge_line = {"kernel": "lse_merge_kernel (standalone pa_lse_merge)", "ms": round(mms, 5),
+                      "bytes": mbytes, "gbs": round(mbytes / (mms * 1e-3) / 1e9, 1),
+                      "frac_of_hbm": round(mbytes / (mms * 1e-3) / 1e9 / hbm_peak, 4),
+                      "peak_source": f"{hbm_kind} HBM copy"}
+
     # end to end through the public API with host buffers (rank-local)
     e2e = None
     if not args.profile:
@@ -363,6 +387,7 @@ def run_ours(args, rank, world, device):
             "e2e": e2e,
             "roofline": roof,
             "permute": perm_line,
+            "merge": merge_line,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
