@@ -323,33 +323,59 @@ def run_ours(args, rank, world, device):
                       "frac_of_hbm": round(mbytes / (mms * 1e-3) / 1e9 / hbm_peak, 4),
                       "peak_source": f"{hbm_kind} HBM copy"}
 
-    # end to end through the public API with host buffers (rank-local)
+    # End to end through the public API with host buffers (rank-local).  Every step
+    # copies its Q, K, V from pinned host memory and reads its O and LSE back; the
+    # steps are pipelined over three streams (H2D of one step, compute of the next
+    # older, D2H of the one before) with double-buffered device and host tensors,
+    # as a serving loop would run them.
     e2e = None
     if not args.profile:
         hq = [x.cpu().pin_memory() for x in bufs[0]]
-        ho = torch.empty(B * H, N, D, dtype=torch.bfloat16).pin_memory()
-        hl = torch.empty(B * H, N, dtype=torch.float32).pin_memory()
-        e2e_steps = max(5, min(args.steps, 50))
-        for i in range(2):
-            qd, kd, vd = (x.to(device, non_blocking=True) for x in hq)
-            o, lse = pipe.step(qd, kd, vd)
-            ho.copy_(o, non_blocking=True)
-            hl.copy_(lse, non_blocking=True)
+        ho = [torch.empty(B * H, N, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+        hl = [torch.empty(B * H, N, dtype=torch.float32).pin_memory() for _ in range(2)]
+        din = [[torch.empty_like(x, device=device) for x in bufs[0]] for _ in range(2)]
+        dout = [(torch.empty(B * H, N, D, device=device, dtype=torch.bfloat16),
+                 torch.empty(B * H, N, device=device, dtype=torch.float32)) for _ in range(2)]
+        s_in, s_comp, s_out = (torch.cuda.Stream(device) for _ in range(3))
+        ev = lambda: torch.cuda.Event()
+        in_ready, comp_done, out_done = ([ev(), ev()] for _ in range(3))
+        for x in comp_done + out_done:
+            x.record(torch.cuda.current_stream(device))
+
+        def e2e_step(i):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(comp_done[b])            # step i-2 has read din[b]
+                for d_, h_ in zip(din[b], hq):
+                    d_.copy_(h_, non_blocking=True)
+                in_ready[b].record(s_in)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(in_ready[b])
+                s_comp.wait_event(out_done[b])           # step i-2's O has left dout[b]
+                pipe.step(*din[b], *dout[b])
+                comp_done[b].record(s_comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(comp_done[b])
+                ho[b].copy_(dout[b][0], non_blocking=True)
+                hl[b].copy_(dout[b][1], non_blocking=True)
+                out_done[b].record(s_out)
+
+        e2e_steps = max(6, min(args.steps, 50))
+        for i in range(4):
+            e2e_step(i)
         torch.cuda.synchronize(device)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        e0.record(s_in)
         for i in range(e2e_steps):
-            qd, kd, vd = (x.to(device, non_blocking=True) for x in hq)
-            o, lse = pipe.step(qd, kd, vd)
-            ho.copy_(o, non_blocking=True)
-            hl.copy_(lse, non_blocking=True)
-        e1.record()
+            e2e_step(i)
+        e1.record(s_out)
         torch.cuda.synchronize(device)
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, device)
         e2e = {"value": round(aggregate_tflops(flops, world, e2e_ms), 3), "unit": "TFLOP/s",
                "ms_per_step": round(e2e_ms, 4),
                "h2d_bytes_per_step": 3 * B * H * N * D * 2,
-               "d2h_bytes_per_step": B * H * N * D * 2 + B * H * N * 4}
+               "d2h_bytes_per_step": B * H * N * D * 2 + B * H * N * 4,
+               "pipelined": "H2D / compute / D2H of consecutive steps on three streams"}
 
     peak, peak_sus, hbm, peak_kind = _peaks()
     roof = None
