@@ -299,6 +299,29 @@ def run_ours(args, rank, world, device):
                      "peak_source": f"{hbm_kind} HBM copy"}
         del pouts
 
+    # the block index (pa_block_index on the device, once per mask): integer work,
+    # one classification per BQ x A tile; CUDA events over repeated builds
+    bi_line = None
+    if pipe.split is None:
+        from polyhedral_b200 import blockindex, masks_gpu
+        bmask = masks_gpu.numpy_mask(pipe.name)
+        build = lambda: blockindex.build_device(bmask, N, pipe.BQ, pipe.A, perm_q=pipe.perm,
+                                                perm_kv=pipe.perm, device=device)
+        for _ in range(3):
+            build()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        breps = 20
+        for _ in range(breps):
+            build()
+        e1.record()
+        torch.cuda.synchronize(device)
+        bus = e0.elapsed_time(e1) / breps * 1e3
+        tiles = (N // pipe.BQ) * (N // pipe.A)
+        bi_line = {"kernel": "block_index_kernel (pa_block_index)", "us": round(bus, 2),
+                   "tiles": tiles, "tiles_per_s": round(tiles / (bus * 1e-6), 1),
+                   "note": "per build incl. output allocation; exact (bit-exact vs the reference)"}
+
     # the standalone LSE merge (pa_lse_merge), HBM-bound; the c5 step itself merges
     # in the attention epilogue instead
     merge_line = None
@@ -414,6 +437,7 @@ def run_ours(args, rank, world, device):
             "roofline": roof,
             "permute": perm_line,
             "merge": merge_line,
+            "block_index": bi_line,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
