@@ -2,7 +2,8 @@
 // dead / full / partial and writes the reference's BlockIndex arrays
 // (gpu/blockindex.py:32-51) without materialising the N x N mask.
 //
-// One CTA per query block.  Each warp takes column tiles in turn.  A tile is
+// One CTA per query block.  Each warp takes column tiles in turn; a column
+// permutation is staged in shared memory first when it fits.  A tile is
 // first decided from bounds alone -- the min/max original coordinate of its rows
 // and columns and, for lattice kinds, whether all rows (columns) share one
 // residue modulo the lattice stride, which makes the lattice term constant over
@@ -109,10 +110,14 @@ __global__ void __launch_bounds__(kThreads)
 block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ perm_q,
                    const int32_t* __restrict__ perm_kv, const uint8_t* __restrict__ dense,
                    int32_t* __restrict__ kv_idx, int kv_stride, int32_t* __restrict__ kv_num,
-                   int8_t* __restrict__ kv_partial, unsigned long long* __restrict__ stats) {
+                   int8_t* __restrict__ kv_partial, unsigned long long* __restrict__ stats,
+                   int stage_kv) {
   extern __shared__ __align__(16) uint8_t smem[];
   int* rows_i = reinterpret_cast<int*>(smem);                 // [BQ]
   uint8_t* flags = smem + ((BQ * 4 + 15) & ~15);              // [nk]
+  // perm_kv staged once per CTA when it fits: the per-tile column reads below are
+  // then shared-memory reads instead of dependent global round trips
+  int* cols_s = reinterpret_cast<int*>(flags + ((N / A + 15) & ~15));   // [N] when stage_kv
   __shared__ int s_warp[kWarps];
   __shared__ int s_red[4];
   __shared__ unsigned long long s_live;
@@ -129,6 +134,10 @@ block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ 
     const int row = rb * BQ + r;
     rows_i[r] = perm_q ? perm_q[row] : row;
   }
+  if (stage_kv) {
+    for (int c = threadIdx.x; c < N; c += kThreads) cols_s[c] = perm_kv[c];
+  }
+  const int32_t* cols = stage_kv ? cols_s : perm_kv;   // NULL: identity columns
   __syncthreads();
 
   // Row-block summary: min / max original row, and residue uniformity mod `mod`.
@@ -158,10 +167,10 @@ block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ 
     int cls = 3;
     if (!dense) {
       int mn = INT_MAX, mx = INT_MIN, uni = 1;
-      const int j0 = perm_kv ? perm_kv[c0] : c0;
+      const int j0 = cols ? cols[c0] : c0;
       const int jres = mod > 1 ? j0 % mod : 0;
       for (int c = lane; c < A; c += 32) {
-        const int j = perm_kv ? perm_kv[c0 + c] : c0 + c;
+        const int j = cols ? cols[c0 + c] : c0 + c;
         mn = min(mn, j); mx = max(mx, j);
         if (mod > 1 && j % mod != jres) uni = 0;
       }
@@ -187,7 +196,7 @@ block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ 
         if (dense) {
           lv = dense[(size_t)(rb * BQ + r) * N + c0 + c] != 0;
         } else {
-          const int j = perm_kv ? perm_kv[c0 + c] : c0 + c;
+          const int j = cols ? cols[c0 + c] : c0 + c;
           lv = pred_live(pred, rows_i[r], j);
         }
         any |= lv; all &= lv; cnt += lv;
@@ -249,14 +258,17 @@ int launch_block_index(const Pred& pred, const uint8_t* dense, int32_t N, int32_
     return fail(PA_ERR_UNSUPPORTED, "%s: N/A=%d (max %d) or BQ=%d (max %d) too large", who,
                 N / A, kMaxTilesPerRow, BQ, kMaxBQ);
   PA_CUDA(cudaMemsetAsync(stats, 0, 4 * sizeof(int64_t), stream), who);
-  const size_t smem = ((size_t)(BQ * 4 + 15) & ~size_t(15)) + (size_t)(N / A);
+  const size_t base = ((size_t)(BQ * 4 + 15) & ~size_t(15)) + (((size_t)(N / A) + 15) & ~size_t(15));
+  // stage perm_kv in shared memory when it fits in what a CTA can have
+  const int stage_kv = (perm_kv && !dense && base + (size_t)N * 4 <= 200 * 1024) ? 1 : 0;
+  const size_t smem = base + (stage_kv ? (size_t)N * 4 : 0);
   if (smem > 48 * 1024) {
     PA_CUDA(cudaFuncSetAttribute(block_index_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem), who);
   }
   block_index_kernel<<<N / BQ, kThreads, smem, stream>>>(
       pred, N, BQ, A, perm_q, perm_kv, dense, kv_idx, kv_stride, kv_num, kv_partial,
-      reinterpret_cast<unsigned long long*>(stats));
+      reinterpret_cast<unsigned long long*>(stats), stage_kv);
   return check_launch(who);
 }
 
