@@ -175,8 +175,9 @@ __device__ __forceinline__ uint32_t range_bits(int lo, int hi, int base) {
 // original indices form the progression j0 + c*dj (dj >= 1), for the row with
 // original index i = j0 + e.  With d = e - c*dj decreasing in c, every kind is a
 // union of at most two ranges of c, and a lattice term (d % m == 0) is constant
-// over the segment when m divides dj.  Returns false when it is not (the caller
-// then evaluates element by element).
+// over the segment when m divides dj, and every m-th column when dj = 1 and m is a
+// power of two.  Returns false otherwise (the caller then evaluates element by
+// element).
 __device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, int dj, int sh,
                                                  int base, int len, uint32_t& out) {
   // floor(a / dj): an arithmetic shift when dj is a power of two (sh >= 0)
@@ -185,7 +186,30 @@ __device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, i
   int lo1 = 0, hi1 = -1, lo2 = 0, hi2 = -1;
   bool lattice = false;
   if (p.mod > 0) {
-    if (!divisible(dj, p.mod, p.inv_mod)) return false;
+    if (!divisible(dj, p.mod, p.inv_mod)) {
+      // Unit column step (no permutation) and a power-of-two modulus: the lattice
+      // columns are every mod-th one, a shifted periodic pattern.
+      if (dj != 1 || p.mod > 32 || (p.mod & (p.mod - 1))) return false;
+      const uint32_t pat = p.mod == 2 ? 0x55555555u : p.mod == 4 ? 0x11111111u
+                           : p.mod == 8 ? 0x01010101u : p.mod == 16 ? 0x00010001u : 1u;
+      const uint32_t lat = e >= 0 ? pat << ((e - base) & (p.mod - 1)) : 0u;
+      int hi = cz;
+      uint32_t near = 0u;
+      switch (p.kind) {
+        case PA_DILATED:
+          break;
+        case PA_FAR_STRIDED:
+          hi = min(cz, fdiv(e - p.p0));
+          break;
+        case PA_LOCAL_STRIDED:
+          near = range_bits(fdiv(e - p.p0) + 1, min(cz, len - 1), base);
+          break;
+        default:
+          return false;
+      }
+      out = (range_bits(0, min(hi, len - 1), base) & lat) | near;
+      return true;
+    }
     lattice = e >= 0 && divisible(e, p.mod, p.inv_mod);   // only e >= 0 can reach c <= cz
   }
   switch (p.kind) {
