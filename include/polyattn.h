@@ -68,7 +68,7 @@ typedef struct pa_pred {
 
 /* Message of the last failed call on this host thread ("" if none). */
 PA_API const char* pa_last_error(void);
-/* ABI revision of this header (4); bumped on any incompatible change. */
+/* ABI revision of this header (5); bumped on any incompatible change. */
 PA_API int pa_abi_version(void);
 
 /* ------------------------------------------------------------ block index
@@ -172,6 +172,21 @@ typedef struct pa_attn_args {
                                         the next S runs during the softmax; faster where many
                                         tiles are partial, e.g. lattice and sinks masks).  64
                                         cannot be combined with merge. */
+  /* The reference's class-B traffic emulation (gpu/triton_attn.py:99-128); all zero /
+     one for the ordinary forward.  Same tiles, same predicate, same result: only the
+     way K/V rows are fetched changes. */
+  int32_t gather_kv;                 /* 1: k and v are in ORIGINAL order and row j of the
+                                        kernel order is read from row perm_kv[j] (NULL =
+                                        identity), per tile, by four-row TMA gathers. */
+  int32_t gather_mult;               /* R in 1..16 (0 reads as 1): each K tile also reads
+                                        (R-1) more sets of its A rows, which the result
+                                        does not use (the reference weights them by 0). */
+  int32_t gather_scatter;            /* extra rows of set r: 0 = row(j) + r*A (contiguous),
+                                        1 = perm_kv[j + r*A] (scattered), both mod N.
+                                        The gathered forward needs residue_stride = 0,
+                                        merge = 0, kv_rows 0 or 128, k and v head strides
+                                        that are multiples of their row strides, and a
+                                        16-byte aligned perm_kv. */
 } pa_attn_args;
 
 /* Bytes of device workspace pa_attn_plan / pa_attn_fwd need for these arguments

@@ -39,7 +39,8 @@ class PaAttnArgs(ctypes.Structure):
                 ("kv_stride", c_i32), ("BQ", c_i32), ("A", c_i32),
                 ("perm_q", c_vp), ("perm_kv", c_vp), ("o_row_map", c_vp),
                 ("pred", PaPred), ("scale", c_f32), ("residue_stride", c_i32),
-                ("merge", c_i32), ("kv_rows", c_i32)]
+                ("merge", c_i32), ("kv_rows", c_i32),
+                ("gather_kv", c_i32), ("gather_mult", c_i32), ("gather_scatter", c_i32)]
 
 
 class PaMergeArgs(ctypes.Structure):
@@ -73,7 +74,7 @@ SIGNATURES = {
     "pa_lse_merge": (ctypes.c_int, [ctypes.POINTER(PaMergeArgs), c_vp]),
 }
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _lib = None
 

@@ -22,9 +22,15 @@ disjoint mask on the same rows and merges this one into them in the epilogue
 (log-sum-exp merge, as ``merge.lse_merge``), so a split runs without a merge pass;
 ``kv_rows=64`` selects the 64-row super-tile kernel (S double-buffered in TMEM:
 faster where many tiles are partial, slower on mostly full tiles; not with
-``merge``).  The reference's class-B emulation
-knobs (``gather_kv``, ``gather_mult``, ``gather_scatter``) are rejected when set;
-``num_warps`` / ``num_stages`` are accepted and ignored.
+``merge``).  ``num_warps`` / ``num_stages`` are accepted and ignored.
+
+The reference's class-B traffic emulation (gpu/triton_attn.py:99-128) keeps its
+meaning: ``gather_kv=True`` takes k and v in ORIGINAL order and reads row j of the
+kernel order from row ``perm_kv[j]`` per tile (four-row TMA gathers), so the result
+equals the one on physically permuted k / v; ``gather_mult=R`` makes every K tile
+read R - 1 more sets of A rows that the result does not use, rows ``row(j) + r*A``
+(``gather_scatter=False``) or ``perm_kv[j + r*A]`` (``gather_scatter=True``),
+mod N.  Not with ``residue_stride``, ``merge`` or ``kv_rows=64``.
 """
 import ctypes
 
@@ -120,10 +126,9 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
                            check=False, residue_stride=0, merge=False, kv_rows=0):
     """q, k, v: [BH, N, D] (bf16 or fp16, D in {64, 128}), on one CUDA device.
     Returns o [BH, N, D] (same dtype), or (o, lse) with ``return_lse``."""
-    if gather_kv or gather_mult != 1:
-        raise NotImplementedError(
-            "gather_kv / gather_mult emulate class-B traffic in the reference "
-            "(gpu/triton_attn.py:99-128); they are not part of this kernel")
+    gather_mult = max(int(gather_mult), 1)     # <= 1 reads no extra rows, as the reference
+    if gather_mult > 16:
+        raise ValueError(f"gather_mult={gather_mult}: at most 16")
     BH, N, D = q.shape
     assert N % BQ == 0 and N % A == 0, "cost model and kernel both assume this"
     assert k.shape == v.shape == q.shape
@@ -184,6 +189,9 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     a.residue_stride = residue_stride
     a.merge = 1 if merge else 0
     a.kv_rows = int(kv_rows or 0)
+    a.gather_kv = 1 if gather_kv else 0
+    a.gather_mult = gather_mult
+    a.gather_scatter = 1 if gather_scatter else 0
     ws = plan.workspace
     _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
               _lib.stream_handle(dev))

@@ -234,6 +234,29 @@ int make_tmap(CUtensorMap* m, const void* base, int dtype, int BH, int N, int D,
   return PA_OK;
 }
 
+// The reference's class-B emulation knobs are set (gather_kv, or a row multiplier).
+bool gathered(const pa_attn_args* a) { return a->gather_kv || a->gather_mult > 1; }
+
+// [BH * rows_per_head][D] 16-bit view of K or V for four-row gathers: box = 64 columns
+// x 1 row, 128-byte swizzle; row j of head b is row b * rows_per_head + j.
+int make_tmap_gather(CUtensorMap* m, const void* base, int dtype, int BH, int N, int D,
+                     long long row_stride, long long bh_stride, const char* name) {
+  EncodeFn enc = get_encode();
+  if (!enc) return fail(PA_ERR_CUDA, "pa_attn_fwd: cuTensorMapEncodeTiled unavailable");
+  const long long per_head = bh_stride / row_stride;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)((long long)(BH - 1) * per_head + N)};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  cuuint32_t box[2] = {64, 1}, estr[2] = {1, 1};
+  CUresult r = enc(m, dtype == PA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PA_ERR_ARG, "pa_attn_fwd: gather tensor map for %s rejected (CUresult %d): "
+                "check 16-byte alignment of the base and strides", name, (int)r);
+  return PA_OK;
+}
+
 int check_args(const pa_attn_args* a, const char* who) {
   PA_CHECK_ARG(a != nullptr, "%s: null args", who);
   PA_CHECK_ARG(a->q && a->k && a->v && a->o, "%s: null q/k/v/o", who);
@@ -258,6 +281,30 @@ int check_args(const pa_attn_args* a, const char* who) {
   if (a->kv_rows == 64 && a->merge)
     return fail(PA_ERR_UNSUPPORTED, "%s: kv_rows=64 cannot be combined with merge", who);
   PA_CHECK_ARG(!a->merge || a->lse, "%s: merge needs the LSE of the result in place (lse)", who);
+  PA_CHECK_ARG(a->gather_kv == 0 || a->gather_kv == 1, "%s: gather_kv=%d must be 0 or 1", who,
+               a->gather_kv);
+  PA_CHECK_ARG(a->gather_mult >= 0 && a->gather_mult <= 16,
+               "%s: gather_mult=%d must be in 1..16", who, a->gather_mult);
+  PA_CHECK_ARG(a->gather_scatter == 0 || a->gather_scatter == 1,
+               "%s: gather_scatter=%d must be 0 or 1", who, a->gather_scatter);
+  if (gathered(a)) {
+    if (a->residue_stride || a->merge || a->kv_rows == 64)
+      return fail(PA_ERR_UNSUPPORTED, "%s: gather_kv / gather_mult cannot be combined with "
+                  "residue_stride, merge or kv_rows=64", who);
+    PA_CHECK_ARG(!a->perm_kv || aligned(a->perm_kv, 16),
+                 "%s: gathered K/V need a 16-byte aligned perm_kv", who);
+    const int64_t ks[2][2] = {{a->k_bh_stride, a->k_row_stride}, {a->v_bh_stride, a->v_row_stride}};
+    for (int t = 0; t < 2; ++t) {
+      const int64_t bs = ks[t][0], rw = ks[t][1];
+      if (rw <= 0 || bs < 0 || bs % rw != 0)
+        return fail(PA_ERR_UNSUPPORTED, "%s: gathered K/V need %s head stride %lld to be a "
+                    "multiple of its row stride %lld", who, t ? "v" : "k", (long long)bs,
+                    (long long)rw);
+      if ((int64_t)(a->BH - 1) * (bs / rw) + a->N > INT32_MAX)
+        return fail(PA_ERR_UNSUPPORTED, "%s: gathered K/V: %s spans more than 2^31 rows", who,
+                    t ? "v" : "k");
+    }
+  }
   if (a->residue_stride != 0) {
     const int rs = a->residue_stride;
     PA_CHECK_ARG(rs >= 1 && a->N % rs == 0, "%s: residue_stride=%d must divide N=%d", who, rs,
@@ -281,12 +328,22 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   if ((rc = make_tmap(&tq, a->q, a->dtype, a->BH, a->N, a->D, a->q_row_stride, a->q_bh_stride,
                       BM, rs, "q")))
     return rc;
-  if ((rc = make_tmap(&tk, a->k, a->dtype, a->BH, a->N, a->D, a->k_row_stride, a->k_bh_stride,
-                      L, rs, "k")))
-    return rc;
-  if ((rc = make_tmap(&tv, a->v, a->dtype, a->BH, a->N, a->D, a->v_row_stride, a->v_bh_stride,
-                      L, rs, "v")))
-    return rc;
+  const bool gather = gathered(a);
+  if (gather) {
+    if ((rc = make_tmap_gather(&tk, a->k, a->dtype, a->BH, a->N, a->D, a->k_row_stride,
+                               a->k_bh_stride, "k")))
+      return rc;
+    if ((rc = make_tmap_gather(&tv, a->v, a->dtype, a->BH, a->N, a->D, a->v_row_stride,
+                               a->v_bh_stride, "v")))
+      return rc;
+  } else {
+    if ((rc = make_tmap(&tk, a->k, a->dtype, a->BH, a->N, a->D, a->k_row_stride,
+                        a->k_bh_stride, L, rs, "k")))
+      return rc;
+    if ((rc = make_tmap(&tv, a->v, a->dtype, a->BH, a->N, a->D, a->v_row_stride,
+                        a->v_bh_stride, L, rs, "v")))
+      return rc;
+  }
   Pred pred;
   if ((rc = make_pred(&a->pred, &pred, "pa_attn_fwd"))) return rc;
   PA_CHECK_ARG(aligned(a->o, 16) && a->o_row_stride % 8 == 0 && a->o_bh_stride % 8 == 0,
@@ -313,6 +370,11 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   P.idesc_qk = make_idesc_f16(fmt, BM, bn, 0, 0);
   P.idesc_pv = make_idesc_f16(fmt, BM, a->D, 0, 1);
   P.total_items = pv.npairs * a->BH;
+  P.g_kbh = gather ? (int)(a->k_bh_stride / a->k_row_stride) : 0;
+  P.g_vbh = gather ? (int)(a->v_bh_stride / a->v_row_stride) : 0;
+  P.g_kv = a->gather_kv;
+  P.g_mult = a->gather_mult > 1 ? a->gather_mult : 1;
+  P.g_scatter = a->gather_scatter;
 
   int dev = 0, sms = 148;
   PA_CUDA(cudaGetDevice(&dev), "pa_attn_fwd");
@@ -321,7 +383,10 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
 
   const bool bf16 = a->dtype == PA_BF16;
   int rc2;
-  if (rows64 && a->D == 128)
+  if (gather)
+    rc2 = a->D == 128 ? launch_d128_gather(tq, tk, tv, P, grid, L, bf16, stream)
+                      : launch_d64_gather(tq, tk, tv, P, grid, L, bf16, stream);
+  else if (rows64 && a->D == 128)
     rc2 = rs > 0 ? db::launch_d128_residue(tq, tk, tv, P, grid, L, bf16, stream)
                  : db::launch_d128(tq, tk, tv, P, grid, L, bf16, stream);
   else if (rows64)

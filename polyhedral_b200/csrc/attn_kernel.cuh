@@ -82,6 +82,10 @@ struct FwdParams {
   PlanView pv;
   uint32_t idesc_qk, idesc_pv;
   int total_items;
+  // gathered K/V (gather kernel only): rows per head of the 2-D K / V views, whether
+  // K/V rows go through perm_kv, the row multiplier of the K reads (1 = none) and
+  // whether the extra rows are scattered
+  int g_kbh, g_vbh, g_kv, g_mult, g_scatter;
 };
 
 template <int D>
@@ -98,6 +102,10 @@ struct Smem {
   static constexpr int kEpiOff = (kMiscOff + 32 + 127) & ~127;   // [8 warps][32 rows][128 B]
   static constexpr int kBytes = kEpiOff + 8 * 32 * 128;
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
+  // gathered K/V only: the landing place of the extra rows nobody reads (one
+  // four-row gather: 4 rows x 128 bytes)
+  static constexpr int kDiscardOff = (kBytes + 1023) & ~1023;
+  static constexpr int kAllocGather = kDiscardOff + 512 + 1024;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -289,7 +297,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-template <int D, int L, bool kBf16, bool kRS, bool kMerge>
+template <int D, int L, bool kBf16, bool kRS, bool kMerge, bool kGather = false>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const FwdParams P) {
@@ -361,7 +369,136 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // Teardown: let every copy issued into the ring and the Q tiles land before the
+    // CTA can exit.  A phase that completed long ago also satisfies the parity
+    // test, so this only ever waits on copies still in flight.
+    auto drain_copies = [&](uint32_t kv_g, const int* q_armed) {
+      const uint64_t t0 = globaltimer();
+      for (uint32_t s = 0; s < (uint32_t)NS && s < kv_g; ++s) {
+        const uint32_t uses = (kv_g - s + NS - 1) / NS;   // loads issued into slot s
+        while (!mbar_try_wait(&kv_full[s], (uses - 1) & 1)) {
+          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+        }
+      }
+      for (int h = 0; h < 2; ++h) {
+        if (q_armed[h] == 0) continue;
+        while (!mbar_try_wait(&q_full[h], (q_armed[h] - 1) & 1)) {
+          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+        }
+      }
+    };
+    if constexpr (kGather) {
+      // Gathered K/V rows (the reference's GATHER_KV / GATHER_MULT knobs,
+      // gpu/triton_attn.py:99-128): row j of the kernel order is read from row
+      // perm_kv[j] of K and V left in original order (row j itself without
+      // gather_kv), four rows per tile::gather4 copy.  Every lane issues the copies
+      // of its own 4-row group of each super-tile; lane 0 owns the schedule and the
+      // barriers and broadcasts its decisions, so the warp stays converged.  With
+      // g_mult = R > 1 each K tile also reads (R - 1) more row sets -- rows
+      // row(j) + r A (contiguous) or perm_kv[j + r A] (scattered), mod N -- into a
+      // discard buffer: the reference weights them by zero, so the result is the
+      // same and only their traffic is paid.
+      int qi = 0;
+      int q_armed[2] = {0, 0};
+      uint32_t kv_g = 0;
+      uint32_t ring = 0;
+      const int grp = lane * 4;                    // this lane's rows of a super-tile
+      const int sg_l = grp / L, t_l = grp - (grp / L) * L;
+      const uint32_t k_bytes = (uint32_t)P.g_mult * SM::kTileBytes;
+      const int32_t* perm = P.perm_kv;
+      uint8_t* sDiscard = smem + SM::kDiscardOff;
+      auto rows4 = [&](const int32_t* pm, int j) -> int4 {   // pm[j..j+3], identity if null
+        if (pm) return __ldg(reinterpret_cast<const int4*>(pm + j));
+        return make_int4(j, j + 1, j + 2, j + 3);
+      };
+      while (true) {
+        int it = -1, ok = 1;
+        if (lane == 0) {
+          it = atomicAdd(P.pv.sched, 1);
+          if (it >= P.total_items || *s_abort) it = -1;
+          const uint32_t rs = ring & 1;
+          if (ring >= 2 &&
+              !mbar_wait(&item_empty[rs], ((ring >> 1) - 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM)) {
+            ok = 0;
+          } else {
+            s_item[rs] = it;
+            mbar_arrive(&item_full[rs]);
+          }
+        }
+        ++ring;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        it = __shfl_sync(0xffffffffu, it, 0);
+        if (!ok || it < 0) break;
+        const int p = __ldg(P.pv.order + it / P.BH);
+        const int bh = it - (it / P.BH) * P.BH;
+        const int cnt = __ldg(P.pv.pair_cnt + p);
+        const int nsup = num_super<L>(P, cnt);
+        if (nsup == 0) continue;
+        const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
+        const uint8_t* sts = P.pv.status + (size_t)p * P.pv.cap;
+        if (lane == 0) {
+          for (int h = 0; h < 2; ++h) {
+            if (qi > 0 && !mbar_wait(&q_empty[h], (qi - 1) & 1, s_abort, err, DEV_TIMEOUT_Q)) {
+              ok = 0;
+              break;
+            }
+            mbar_arrive_expect_tx(&q_full[h], SM::kTileBytes);
+            ++q_armed[h];
+            const int qr = p * 2 * BM + h * BM;
+            for (int c = 0; c < kChunks; ++c)
+              tma_load_3d(sQ + h * SM::kTileBytes + c * kRegion, &tm_q, &q_full[h], c * 64, qr,
+                          bh);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        const int kb = bh * P.g_kbh, vb = bh * P.g_vbh;   // row 0 of this head in the 2-D views
+        for (int u = 0; u < nsup && ok; ++u) {
+          const SegInfo si = seg_info<L>(P, ent, sts, cnt, u, sg_l);
+          // a padding segment (past the listed tiles, masked as dead) reads any valid rows
+          const int j = si.row0 < P.N ? si.row0 + t_l : t_l % P.N;
+          const int4 b = rows4(P.g_kv ? perm : nullptr, j);
+          for (int kv = 0; kv < 2; ++kv) {
+            const uint32_t slot = kv_g % NS;
+            if (lane == 0) {
+              if (kv_g >= (uint32_t)NS &&
+                  !mbar_wait(&kv_empty[slot], ((kv_g / NS) - 1) & 1, s_abort, err,
+                             DEV_TIMEOUT_KV))
+                ok = 0;
+              else
+                mbar_arrive_expect_tx(&kv_full[slot], kv == 0 ? k_bytes : SM::kTileBytes);
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            ++kv_g;
+            uint8_t* dst = sKV + slot * SM::kTileBytes + grp * 128;
+            const void* tm = kv == 0 ? (const void*)&tm_k : (const void*)&tm_v;
+            const int base = kv == 0 ? kb : vb;
+            for (int c = 0; c < kChunks; ++c)
+              tma_gather4(dst + c * kRegion, tm, &kv_full[slot], c * 64, base + b.x, base + b.y,
+                          base + b.z, base + b.w);
+            if (kv == 0) {
+              for (int r = 1; r < P.g_mult; ++r) {
+                int4 e;
+                if (P.g_scatter) {
+                  e = rows4(perm, (j + r * P.A) % P.N);
+                } else {
+                  const int sh = r * P.A;
+                  e = make_int4((b.x + sh) % P.N, (b.y + sh) % P.N, (b.z + sh) % P.N,
+                                (b.w + sh) % P.N);
+                }
+                for (int c = 0; c < kChunks; ++c)
+                  tma_gather4(sDiscard, &tm_k, &kv_full[slot], c * 64, kb + e.x, kb + e.y,
+                              kb + e.z, kb + e.w);
+              }
+            }
+          }
+        }
+        if (!ok) break;
+        ++qi;
+      }
+      if (lane == 0) drain_copies(kv_g, q_armed);
+    } else if (lane == 0) {
       int qi = 0;
       int q_armed[2] = {0, 0};
       uint32_t kv_g = 0;
@@ -433,22 +570,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         }
         ++qi;
       }
-      // Teardown: let every copy this thread issued land before the CTA can exit.
-      // A phase that completed long ago also satisfies the parity test, so this
-      // only ever waits on copies still in flight.
-      const uint64_t t0 = globaltimer();
-      for (uint32_t s = 0; s < (uint32_t)NS && s < kv_g; ++s) {
-        const uint32_t uses = (kv_g - s + NS - 1) / NS;   // loads issued into slot s
-        while (!mbar_try_wait(&kv_full[s], (uses - 1) & 1)) {
-          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
-        }
-      }
-      for (int h = 0; h < 2; ++h) {
-        if (q_armed[h] == 0) continue;
-        while (!mbar_try_wait(&q_full[h], (q_armed[h] - 1) & 1)) {
-          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
-        }
-      }
+      drain_copies(kv_g, q_armed);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -952,28 +1074,30 @@ PA_DECLARE_LAUNCH(launch_d128_merge)
 PA_DECLARE_LAUNCH(launch_d128_residue_merge)
 PA_DECLARE_LAUNCH(launch_d64_merge)
 PA_DECLARE_LAUNCH(launch_d64_residue_merge)
+PA_DECLARE_LAUNCH(launch_d128_gather)
+PA_DECLARE_LAUNCH(launch_d64_gather)
 #undef PA_DECLARE_LAUNCH
 
 // Body of the launchers: pick the instantiation for (L, dtype).
-template <int D, bool kRS, bool kMerge>
+template <int D, bool kRS, bool kMerge, bool kGather = false>
 int launch_family(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P, int grid,
                   int L, bool bf16, cudaStream_t stream) {
   auto go = [&](auto kernel) -> int {
-    const int smem = Smem<D>::kAlloc;
+    const int smem = kGather ? Smem<D>::kAllocGather : Smem<D>::kAlloc;
     PA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
             "pa_attn_fwd");
     kernel<<<grid, kThreads, smem, stream>>>(tq, tk, tv, P);
     return PA_OK;
   };
   switch (L) {
-    case 16: return bf16 ? go(attn_fwd_kernel<D, 16, true, kRS, kMerge>)
-                         : go(attn_fwd_kernel<D, 16, false, kRS, kMerge>);
-    case 32: return bf16 ? go(attn_fwd_kernel<D, 32, true, kRS, kMerge>)
-                         : go(attn_fwd_kernel<D, 32, false, kRS, kMerge>);
-    case 64: return bf16 ? go(attn_fwd_kernel<D, 64, true, kRS, kMerge>)
-                         : go(attn_fwd_kernel<D, 64, false, kRS, kMerge>);
-    default: return bf16 ? go(attn_fwd_kernel<D, 128, true, kRS, kMerge>)
-                         : go(attn_fwd_kernel<D, 128, false, kRS, kMerge>);
+    case 16: return bf16 ? go(attn_fwd_kernel<D, 16, true, kRS, kMerge, kGather>)
+                         : go(attn_fwd_kernel<D, 16, false, kRS, kMerge, kGather>);
+    case 32: return bf16 ? go(attn_fwd_kernel<D, 32, true, kRS, kMerge, kGather>)
+                         : go(attn_fwd_kernel<D, 32, false, kRS, kMerge, kGather>);
+    case 64: return bf16 ? go(attn_fwd_kernel<D, 64, true, kRS, kMerge, kGather>)
+                         : go(attn_fwd_kernel<D, 64, false, kRS, kMerge, kGather>);
+    default: return bf16 ? go(attn_fwd_kernel<D, 128, true, kRS, kMerge, kGather>)
+                         : go(attn_fwd_kernel<D, 128, false, kRS, kMerge, kGather>);
   }
 }
 

@@ -104,6 +104,18 @@ PA_DEV void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int c0, int 
       ::"r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+// Four-row gather (tile::gather4, no multicast) through a 2-D map whose box is 64
+// columns x 1 row: rows r0..r3 at column c0 land as four consecutive 128-byte rows
+// at dst (swizzled by the map's mode, which follows the shared-memory address).
+PA_DEV void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int c0, int r0, int r1,
+                        int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2),
+        "r"(r3)
+      : "memory");
+}
 PA_DEV void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

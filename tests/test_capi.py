@@ -89,6 +89,25 @@ def test_argument_errors_before_launch(lib):
     assert lib.pa_attn_workspace_size(ctypes.byref(a)) > 0
     # workspace too small
     assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 16, None) == _lib.PA_ERR_ARG
+    # gathered K/V: multiplier range, combinations, head stride vs row stride
+    a.k_row_stride = a.v_row_stride = 128
+    a.k_bh_stride = a.v_bh_stride = 1024 * 128
+    a.gather_kv, a.gather_mult = 1, 17
+    assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20, None) == _lib.PA_ERR_ARG
+    assert b"gather_mult=17" in lib.pa_last_error()
+    a.gather_mult, a.residue_stride = 4, 4
+    assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20,
+                           None) == _lib.PA_ERR_UNSUPPORTED
+    a.residue_stride, a.kv_rows = 0, 64
+    assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20,
+                           None) == _lib.PA_ERR_UNSUPPORTED
+    a.kv_rows, a.k_bh_stride = 0, 100
+    assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20,
+                           None) == _lib.PA_ERR_UNSUPPORTED
+    assert b"multiple of its row stride" in lib.pa_last_error()
+    a.k_bh_stride, a.perm_kv = 1024 * 128, 20
+    assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20, None) == _lib.PA_ERR_ARG
+    assert b"16-byte aligned perm_kv" in lib.pa_last_error()
     # merge: null pointers
     m = _lib.PaMergeArgs()
     assert lib.pa_lse_merge(ctypes.byref(m), None) == _lib.PA_ERR_ARG
@@ -105,8 +124,8 @@ def test_python_layer_raises_without_gpu_work():
     q = torch.zeros(1, 256, 128, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="GPU only"):
         attention.block_sparse_attention(q, q, q, None, None, None, 1, 128, 0, 0, 128, 32)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="gather_mult"):
         attention.block_sparse_attention(q, q, q, None, None, None, 1, 128, 0, 0, 128, 32,
-                                         gather_mult=2)
+                                         gather_mult=17)
     with pytest.raises(AssertionError):
         attention.block_sparse_attention(q, q, q, None, None, None, 1, 128, 0, 0, 100, 32)
