@@ -1,7 +1,7 @@
 """Benchmark of the block-sparse attention forward path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c2|c3|c4|c5]
+                    [--workload c1|c2|c3|c3-rp8|c4|c5]
 
 Metric: effective TFLOP/s over LIVE mask elements,
 4 * D * live * B * H per forward, with ms per forward.  Default workload c2
@@ -42,8 +42,13 @@ WORKLOADS = {
            "c1: window-128, B1 H4 N1024 D64 (fp32 inputs cast to bf16), 128x32 tiles"),
     "c2": (1, 16, 8192, 128, "dilated-4", 4, 128, 32, 1,
            "c2: dilated-4 + residue-perm-4, 128x32 tiles, B1 H16 N8192 D128 bf16"),
-    "c3": (2, 16, 16384, 128, "local64+str8", 8, 128, 32, 2,
-           "c3: local64+str8 + residue-perm-8, 128x32 tiles, 64-row KV super-tiles, B2 H16 N16384 D128 bf16"),
+    "c3": (2, 16, 16384, 128, "local64+str8", 8, 128, 64, 2,
+           "c3: local64+str8 as window-64 (identity, 128x64, 64-row KV super-tiles) + far64+str8 "
+           "(residue-perm-8, 128x64) split, LSE merge fused into the second part's epilogue, "
+           "B2 H16 N16384 D128 bf16"),
+    "c3-rp8": (2, 16, 16384, 128, "local64+str8", 8, 128, 32, 2,
+               "c3 in one basis: local64+str8 + residue-perm-8, 128x32 tiles, 64-row KV "
+               "super-tiles, B2 H16 N16384 D128 bf16"),
     "c4": (4, 32, 8192, 128, "sinks4+win512", 0, 128, 32, 3,
            "c4: sinks4+win512, 128x32 tiles, 64-row KV super-tiles, B4 H32 N8192 D128 bf16"),
     "c5": (2, 64, 32768, 128, "local1024+str16", 16, 128, 64, 4,
@@ -52,7 +57,17 @@ WORKLOADS = {
 }
 # KV rows per super-tile of the attention kernel, per workload (default 128); the
 # 64-row kernel wins where many tiles are partial (lattice and sinks masks)
-KV_ROWS = {"c3": 64, "c4": 64}
+KV_ROWS = {"c3-rp8": 64, "c4": 64}
+# Workloads computed as a disjoint split, part by part: (mask spec name, BQ, A,
+# residue stride, KV rows per super-tile).  The first part writes O / LSE, the
+# second merges into them in its epilogue.  Band + lattice unions split into the
+# band in the identity basis and the lattice beyond it in its residue basis, where
+# each is dense; in one residue basis the band is spread over every off-diagonal
+# block (c3: 2x the tiles).
+SPLITS = {
+    "c3": [("window-64", 128, 64, 0, 64), ("far64+str8", 128, 64, 8, 0)],
+    "c5": [("window-1024", 128, 128, 0, 0), ("far1024+str16", 128, 64, 16, 0)],
+}
 
 
 def _peaks():
@@ -172,10 +187,11 @@ class Pipeline:
         self.spec = masks_gpu.triton_params(name)
         torch.cuda.synchronize(device)
         t0 = time.perf_counter()
-        if wl == "c5":
+        if wl in SPLITS:
+            self.split_names = [pn for pn, *_ in SPLITS[wl]]
             self.split = split.SplitPlan(
-                [split.SplitPart(masks_gpu.numpy_mask("window-1024"), 128, 128, 0),
-                 split.SplitPart(masks_gpu.numpy_mask("far1024+str16"), BQ, A, s)], N, device)
+                [split.SplitPart(masks_gpu.numpy_mask(pn), pbq, pa, ps, pkv)
+                 for pn, pbq, pa, ps, pkv in SPLITS[wl]], N, device)
             self.perm = None
             self.plan = None
         else:
@@ -264,10 +280,29 @@ def run_ours(args, rank, world, device):
     ms_per_step = t_ms / args.steps
     value = aggregate_tflops(flops, world, ms_per_step)
 
-    # dominant kernel alone, CUDA events on the launching stream
+    # dominant kernel alone, CUDA events on the launching stream (for a split: each
+    # part's launch alone, the dominant one by live work reported)
     kernel_ms = None
+    kernel_flops, kernel_name = flops, "attn_fwd_kernel"
     reps = max(args.steps, 20)
-    if pipe.split is None:
+    if pipe.split is not None:
+        from polyhedral_b200 import masks_gpu
+        part_flops = [4.0 * D * masks_gpu.numpy_mask(pn).live_count(N) * B * H
+                      for pn in pipe.split_names]
+        dom = max(range(len(part_flops)), key=lambda i: part_flops[i])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(3):
+            pipe.split.run_part(dom, *bufs[i % nbuf], *outs[i % nbuf])
+        e0.record()
+        for i in range(reps):
+            pipe.split.run_part(dom, *bufs[i % nbuf], *outs[i % nbuf])
+        e1.record()
+        torch.cuda.synchronize(device)
+        kernel_ms = e0.elapsed_time(e1) / reps
+        kernel_flops = part_flops[dom]
+        kernel_name = f"attn_fwd_kernel ({pipe.split_names[dom]} part, merging)" if dom else \
+            f"attn_fwd_kernel ({pipe.split_names[dom]} part)"
+    else:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         for i in range(3):
             pipe.attn_only(*bufs[i % nbuf], *outs[i % nbuf])
@@ -322,7 +357,7 @@ def run_ours(args, rank, world, device):
                    "tiles": tiles, "tiles_per_s": round(tiles / (bus * 1e-6), 1),
                    "note": "per build incl. output allocation; exact (bit-exact vs the reference)"}
 
-    # the standalone LSE merge (pa_lse_merge), HBM-bound; the c5 step itself merges
+    # the standalone LSE merge (pa_lse_merge), HBM-bound; a split step itself merges
     # in the attention epilogue instead
     merge_line = None
     if pipe.split is not None:
@@ -403,11 +438,11 @@ def run_ours(args, rank, world, device):
     peak, peak_sus, hbm, peak_kind = _peaks()
     roof = None
     if kernel_ms is not None:
-        ach = flops / (kernel_ms * 1e-3) / 1e12
+        ach = kernel_flops / (kernel_ms * 1e-3) / 1e12
         traffic = _traffic_from_profiles(wl)
         roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(ach / peak, 4), "traffic": traffic,
-                "kernel": "attn_fwd_kernel", "kernel_ms": round(kernel_ms, 5),
+                "kernel": kernel_name, "kernel_ms": round(kernel_ms, 5),
                 "peak_source": f"{peak_kind} bf16 dense (burst)"}
 
     cpu = None
@@ -427,8 +462,8 @@ def run_ours(args, rank, world, device):
                        "l2": f"inputs rotated over {nbuf} buffer sets ({nbuf * step_bytes >> 20} MiB >= 2x L2)",
                        "index_ms": round(pipe.index_ms, 3),
                        "step": "attention (O, LSE) over the residue permutation applied on the fly, "
-                               "inputs/outputs in original order" if wl != "c5" else
-                               "window part + lattice part (residue-16 on the fly) merging into "
+                               "inputs/outputs in original order" if pipe.split is None else
+                               f"window part + lattice part (residue-{s} on the fly) merging into "
                                "the window part's O / LSE in its epilogue"},
             "pct_bf16_peak": round(value / world / peak, 4),
             "gpu_launches": pipe.launches_per_step() * args.steps,

@@ -16,6 +16,7 @@ SPECS = {
     "causal":          (CAUSAL, 0, 0, 0, lambda: masks.Causal()),
     "window-128":      (WINDOW, 128, 0, 0, lambda: masks.SlidingWindow(128)),
     "window-512":      (WINDOW, 512, 0, 0, lambda: masks.SlidingWindow(512)),
+    "window-64":       (WINDOW, 64, 0, 0, lambda: masks.SlidingWindow(64)),
     "window-1024":     (WINDOW, 1024, 0, 0, lambda: masks.SlidingWindow(1024)),
     "dilated-4":       (DILATED, 4, 0, 0, lambda: masks.Dilated(4)),
     "dilated-8":       (DILATED, 8, 0, 0, lambda: masks.Dilated(8)),
@@ -23,6 +24,7 @@ SPECS = {
     "local256+str8":   (LOCAL_STRIDED, 256, 8, 0, lambda: masks.LocalStrided(256, 8)),
     "local64+str8":    (LOCAL_STRIDED, 64, 8, 0, lambda: masks.LocalStrided(64, 8)),
     "local1024+str16": (LOCAL_STRIDED, 1024, 16, 0, lambda: masks.LocalStrided(1024, 16)),
+    "far64+str8":      (FAR_STRIDED, 64, 8, 0, lambda: masks.FarStrided(64, 8)),
     "far1024+str16":   (FAR_STRIDED, 1024, 16, 0, lambda: masks.FarStrided(1024, 16)),
     "twoband-1024":    (TWOBAND, 128, 1024, 128, lambda: masks.TwoBand(128, 1024)),
     "twoband-1000":    (TWOBAND, 128, 1000, 128, lambda: masks.TwoBand(128, 1000)),

@@ -30,6 +30,7 @@ class SplitPart:
     BQ: int
     A: int
     stride: int = 0         # residue-permutation stride; 0 = identity basis
+    kv_rows: int = 0        # attention kernel's KV super-tile (0/128, or 64: first part only)
 
 
 class SplitPlan:
@@ -40,6 +41,9 @@ class SplitPlan:
         self.N = N
         self.parts = list(parts)
         self.device = torch.device(device)
+        if any(part.kv_rows == 64 for part in self.parts[1:]):
+            raise ValueError("only the first part can use kv_rows=64: later parts merge "
+                             "in their epilogue, which the 64-row kernel does not")
         self.perms, self.indices, self.plans = [], [], []
         for part in self.parts:
             perm = None
@@ -66,17 +70,28 @@ class SplitPlan:
             attention.block_sparse_attention(
                 q, k, v, None, None, None, kind, p0, p1, p2, part.BQ, part.A,
                 scale=scale, residue_stride=part.stride, plan=self.plans[i], return_lse=True,
-                out=o, lse_out=lse, merge=i > 0)
+                out=o, lse_out=lse, merge=i > 0, kv_rows=part.kv_rows)
         return o, lse
+
+    def run_part(self, i, q, k, v, o, lse, scale=None):
+        """Part i alone, as ``run`` launches it (merging into o / lse when i > 0)."""
+        part = self.parts[i]
+        kind, p0, p1, p2 = part.mask.spec
+        return attention.block_sparse_attention(
+            q, k, v, None, None, None, kind, p0, p1, p2, part.BQ, part.A, scale=scale,
+            residue_stride=part.stride, plan=self.plans[i], return_lse=True, out=o,
+            lse_out=lse, merge=i > 0, kv_rows=part.kv_rows)
 
     def live_count(self):
         return sum(int(p.mask.live_count(self.N)) for p in self.parts)
 
 
-def local_strided_split(w, s, N, BQ=128, A=32, stride=None, device="cuda"):
-    """LocalStrided(w, s) = SlidingWindow(w) [identity] + FarStrided(w, s)
-    [residue permutation by `stride`, default s]."""
-    parts = [SplitPart(masks.SlidingWindow(w), BQ, A, 0),
+def local_strided_split(w, s, N, BQ=128, A=32, stride=None, device="cuda", A_window=None,
+                        window_kv_rows=0):
+    """LocalStrided(w, s) = SlidingWindow(w) [identity, tiles BQ x A_window (default
+    A), KV super-tile ``window_kv_rows``] + FarStrided(w, s) [residue permutation by
+    `stride`, default s, tiles BQ x A]."""
+    parts = [SplitPart(masks.SlidingWindow(w), BQ, A_window or A, 0, window_kv_rows),
              SplitPart(masks.FarStrided(w, s), BQ, A, stride or s)]
     return SplitPlan(parts, N, device)
 

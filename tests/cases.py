@@ -9,6 +9,7 @@ SPECS = {
     "causal": (O.CAUSAL, 0, 0, 0),
     "window-128": (O.WINDOW, 128, 0, 0),
     "window-512": (O.WINDOW, 512, 0, 0),
+    "window-64": (O.WINDOW, 64, 0, 0),
     "window-1024": (O.WINDOW, 1024, 0, 0),
     "dilated-4": (O.DILATED, 4, 0, 0),
     "dilated-8": (O.DILATED, 8, 0, 0),
@@ -16,6 +17,7 @@ SPECS = {
     "local256+str8": (O.LOCAL_STRIDED, 256, 8, 0),
     "local64+str8": (O.LOCAL_STRIDED, 64, 8, 0),
     "local1024+str16": (O.LOCAL_STRIDED, 1024, 16, 0),
+    "far64+str8": (O.FAR_STRIDED, 64, 8, 0),
     "far1024+str16": (O.FAR_STRIDED, 1024, 16, 0),
     "twoband-1024": (O.TWOBAND, 128, 1024, 128),
     "twoband-1000": (O.TWOBAND, 128, 1000, 128),

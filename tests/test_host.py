@@ -56,6 +56,23 @@ def test_config5_split_is_a_disjoint_cover():
     assert sum(p.mask.live_count(32768) for p in parts) == union.live_count(32768)
 
 
+def test_config3_split_is_a_disjoint_cover():
+    """Band + lattice (configuration 3) = window-64 (identity) + far64+str8 (residue-8)."""
+    union = masks.LocalStrided(64, 8)
+    parts = [split.SplitPart(masks.SlidingWindow(64), 128, 64, 0, 64),
+             split.SplitPart(masks.FarStrided(64, 8), 128, 64, 8)]
+    assert split.check_disjoint_cover(union, parts, 3000)
+    assert sum(p.mask.live_count(16384) for p in parts) == union.live_count(16384)
+
+
+def test_split_refuses_64_row_merging_part():
+    import pytest
+    with pytest.raises(ValueError, match="first part"):
+        split.SplitPlan([split.SplitPart(masks.SlidingWindow(64), 128, 64, 0),
+                         split.SplitPart(masks.FarStrided(64, 8), 128, 64, 8, 64)], 1024,
+                        device="cpu")
+
+
 def test_flex_mask_mod_far_strided():
     import torch
     M = masks_gpu.dense_bool("far1024+str16", 2048, device="cpu")
