@@ -68,7 +68,7 @@ typedef struct pa_pred {
 
 /* Message of the last failed call on this host thread ("" if none). */
 PA_API const char* pa_last_error(void);
-/* ABI revision of this header (5); bumped on any incompatible change. */
+/* ABI revision of this header (6); bumped on any incompatible change. */
 PA_API int pa_abi_version(void);
 
 /* ------------------------------------------------------------ block index
@@ -187,6 +187,12 @@ typedef struct pa_attn_args {
                                         merge = 0, kv_rows 0 or 128, k and v head strides
                                         that are multiples of their row strides, and a
                                         16-byte aligned perm_kv. */
+  int32_t sched_heads;               /* heads per scheduling group of the forward's work
+                                        items (items of one group run pair by pair, all
+                                        its heads together, longest pair first; groups
+                                        run one after another): 0 or >= BH = one group.
+                                        Groups whose K/V fit in L2 cut DRAM re-reads when
+                                        all heads' K/V do not. */
 } pa_attn_args;
 
 /* Bytes of device workspace pa_attn_plan / pa_attn_fwd need for these arguments

@@ -22,7 +22,10 @@ disjoint mask on the same rows and merges this one into them in the epilogue
 (log-sum-exp merge, as ``merge.lse_merge``), so a split runs without a merge pass;
 ``kv_rows=64`` selects the 64-row super-tile kernel (S double-buffered in TMEM:
 faster where many tiles are partial, slower on mostly full tiles; not with
-``merge``).  ``num_warps`` / ``num_stages`` are accepted and ignored.
+``merge``).  ``sched_heads=G`` runs the work items in groups of G heads, one group
+after another (default: all heads in one group); groups whose K/V fit in L2 cut DRAM
+re-reads when all heads' K/V do not.
+``num_warps`` / ``num_stages`` are accepted and ignored.
 
 The reference's class-B traffic emulation (gpu/triton_attn.py:99-128) keeps its
 meaning: ``gather_kv=True`` takes k and v in ORIGINAL order and reads row j of the
@@ -123,7 +126,8 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
                            gather_mult=1, gather_scatter=True,
                            num_warps=4, num_stages=2, *, return_lse=False,
                            o_row_map=None, plan=None, out=None, lse_out=None,
-                           check=False, residue_stride=0, merge=False, kv_rows=0):
+                           check=False, residue_stride=0, merge=False, kv_rows=0,
+                           sched_heads=0):
     """q, k, v: [BH, N, D] (bf16 or fp16, D in {64, 128}), on one CUDA device.
     Returns o [BH, N, D] (same dtype), or (o, lse) with ``return_lse``."""
     gather_mult = max(int(gather_mult), 1)     # <= 1 reads no extra rows, as the reference
@@ -192,6 +196,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     a.gather_kv = 1 if gather_kv else 0
     a.gather_mult = gather_mult
     a.gather_scatter = 1 if gather_scatter else 0
+    a.sched_heads = int(sched_heads or 0)
     ws = plan.workspace
     _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
               _lib.stream_handle(dev))

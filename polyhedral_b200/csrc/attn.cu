@@ -281,6 +281,7 @@ int check_args(const pa_attn_args* a, const char* who) {
   if (a->kv_rows == 64 && a->merge)
     return fail(PA_ERR_UNSUPPORTED, "%s: kv_rows=64 cannot be combined with merge", who);
   PA_CHECK_ARG(!a->merge || a->lse, "%s: merge needs the LSE of the result in place (lse)", who);
+  PA_CHECK_ARG(a->sched_heads >= 0, "%s: sched_heads=%d < 0", who, a->sched_heads);
   PA_CHECK_ARG(a->gather_kv == 0 || a->gather_kv == 1, "%s: gather_kv=%d must be 0 or 1", who,
                a->gather_kv);
   PA_CHECK_ARG(a->gather_mult >= 0 && a->gather_mult <= 16,
@@ -370,6 +371,8 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   P.idesc_qk = make_idesc_f16(fmt, BM, bn, 0, 0);
   P.idesc_pv = make_idesc_f16(fmt, BM, a->D, 0, 1);
   P.total_items = pv.npairs * a->BH;
+  // heads per scheduling group (all heads unless the caller asks for groups)
+  P.hg = a->sched_heads > 0 && a->sched_heads < a->BH ? a->sched_heads : a->BH;
   P.g_kbh = gather ? (int)(a->k_bh_stride / a->k_row_stride) : 0;
   P.g_vbh = gather ? (int)(a->v_bh_stride / a->v_row_stride) : 0;
   P.g_kv = a->gather_kv;

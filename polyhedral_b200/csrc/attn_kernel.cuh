@@ -82,6 +82,7 @@ struct FwdParams {
   PlanView pv;
   uint32_t idesc_qk, idesc_pv;
   int total_items;
+  int hg;              // heads per scheduling group (BH: one group)
   // gathered K/V (gather kernel only): rows per head of the 2-D K / V views, whether
   // K/V rows go through perm_kv, the row multiplier of the K reads (1 = none) and
   // whether the extra rows are scattered
@@ -143,6 +144,22 @@ struct SegInfo {
   int row0;
   int st;
 };
+
+// Work item `it` -> (pair, head).  Items run in groups of P.hg heads (the last group
+// may have fewer; P.hg = BH by default: one group); inside a group they go pair by
+// pair in the plan's longest-first order, every head of the group for one pair.
+// With small groups the CTAs in flight read the K/V of a few heads only, which stay
+// in L2 while the pairs that share them run.
+__device__ __forceinline__ void item_coords(const FwdParams& P, int it, int& p, int& bh) {
+  const int gsz = P.hg * P.pv.npairs;          // items of a full group
+  const int g = it / gsz;
+  const int h0 = g * P.hg;
+  const int gh = min(P.hg, P.BH - h0);         // heads of this group
+  const int li = it - g * gsz;
+  const int q = li / gh;
+  p = __ldg(P.pv.order + q);
+  bh = h0 + (li - q * gh);
+}
 
 template <int L>
 __device__ __forceinline__ int num_super(const FwdParams& P, int cnt) {
@@ -429,8 +446,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         ok = __shfl_sync(0xffffffffu, ok, 0);
         it = __shfl_sync(0xffffffffu, it, 0);
         if (!ok || it < 0) break;
-        const int p = __ldg(P.pv.order + it / P.BH);
-        const int bh = it - (it / P.BH) * P.BH;
+        int p, bh;
+        item_coords(P, it, p, bh);
         const int cnt = __ldg(P.pv.pair_cnt + p);
         const int nsup = num_super<L>(P, cnt);
         if (nsup == 0) continue;
@@ -515,8 +532,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         mbar_arrive(&item_full[rs]);
         ++ring;
         if (it < 0) break;
-        const int p = __ldg(P.pv.order + it / P.BH);
-        const int bh = it - (it / P.BH) * P.BH;
+        int p, bh;
+        item_coords(P, it, p, bh);
         const int cnt = __ldg(P.pv.pair_cnt + p);
         const int nsup = num_super<L>(P, cnt);
         if (nsup == 0) continue;
@@ -625,7 +642,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         mbar_arrive(&item_empty[rs]);
         ++ring;
         if (it < 0) break;
-        const int p = __ldg(P.pv.order + it / P.BH);
+        int p, bh_unused;
+        item_coords(P, it, p, bh_unused);
         const int nsup = num_super<L>(P, __ldg(P.pv.pair_cnt + p));
         if (nsup == 0) continue;
         ok = mbar_wait(&q_full[0], qi & 1, s_abort, err, DEV_TIMEOUT_Q) &&
@@ -692,8 +710,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       if (lane == 0) mbar_arrive(&item_empty[rs]);
       ++ring;
       if (it < 0) break;
-      const int p = __ldg(P.pv.order + it / P.BH);
-      const int bh = it - (it / P.BH) * P.BH;
+      int p, bh;
+      item_coords(P, it, p, bh);
       const int cnt = __ldg(P.pv.pair_cnt + p);
       const int nsup = num_super<L>(P, cnt);
       const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;

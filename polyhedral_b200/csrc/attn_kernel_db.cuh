@@ -162,8 +162,8 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         mbar_arrive(&item_full[rs]);
         ++ring;
         if (it < 0) break;
-        const int p = __ldg(P.pv.order + it / P.BH);
-        const int bh = it - (it / P.BH) * P.BH;
+        int p, bh;
+        item_coords(P, it, p, bh);
         const int cnt = __ldg(P.pv.pair_cnt + p);
         const int nsup = num_super64<L>(P, cnt);
         if (nsup == 0) continue;
@@ -295,7 +295,8 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         mbar_arrive(&item_empty[rs]);
         ++ring;
         if (it < 0) break;
-        const int p = __ldg(P.pv.order + it / P.BH);
+        int p, bh_unused;
+        item_coords(P, it, p, bh_unused);
         const int nsup = num_super64<L>(P, __ldg(P.pv.pair_cnt + p));
         if (nsup == 0) continue;
         ok = mbar_wait(&q_full[0], qi & 1, s_abort, err, DEV_TIMEOUT_Q) &&
@@ -347,8 +348,8 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       if (lane == 0) mbar_arrive(&item_empty[rs]);
       ++ring;
       if (it < 0) break;
-      const int p = __ldg(P.pv.order + it / P.BH);
-      const int bh = it - (it / P.BH) * P.BH;
+      int p, bh;
+      item_coords(P, it, p, bh);
       const int cnt = __ldg(P.pv.pair_cnt + p);
       const int nsup = num_super64<L>(P, cnt);
       const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;

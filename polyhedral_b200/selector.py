@@ -28,6 +28,14 @@ others: ``offsets_of``).  Every cost is then exact arithmetic on those runs:
 by candidate order); ``select_class_a`` restricts the choice to what the
 kernel executes and returns the residue stride to pass as ``residue_stride``;
 ``prepare`` builds everything the forward needs for that choice on the GPU.
+
+``select_split`` adds the composition the reference only counts
+(src/polyattn/experiments/compose.py:1-24, 36-44): a band + lattice union
+LocalStrided(w, s) is the disjoint union of SlidingWindow(w) and FarStrided(w, s);
+each part takes its own cheapest executable basis, and the split wins when its
+elements are fewer than the best single basis' by more than ``SPLIT_MARGIN``
+(the merge is fused into the second part's epilogue, but it rereads O and LSE).
+``prepare(..., allow_split=True)`` then builds a ``split.SplitPlan``.
 """
 from math import gcd
 
@@ -35,7 +43,10 @@ import numpy as np
 
 __all__ = ["CANDIDATES", "RaggedNotSupported", "offsets_of", "tile_cost", "costs",
            "select", "select_class_a", "is_class_b", "stride_of", "prepare", "ClassAPlan",
-           "costs_device"]
+           "costs_device", "select_split", "SPLIT_MARGIN"]
+
+# A split must compute this fraction fewer elements than the best single basis.
+SPLIT_MARGIN = 0.10
 
 CANDIDATES = (["identity", "shear"]
               + [f"stridefold-{s}" for s in (2, 4, 8)]
@@ -293,10 +304,59 @@ class ClassAPlan:
             residue_stride=self.stride, plan=self.plan, return_lse=return_lse)
 
 
-def prepare(mask, N, BQ, A, device="cuda"):
+def select_split(mask, N, BQ, A):
+    """Single basis vs band + lattice split for a LocalStrided(w, s) mask.
+
+    Returns {"single": (name, stride, elements), "parts": [(mask, name, stride,
+    elements), ...], "split": bool} -- ``split`` True when the parts' elements
+    undercut the single basis by more than ``SPLIT_MARGIN`` -- or None for a mask
+    that is not a band + lattice union."""
+    from . import masks as M
+    spec = getattr(mask, "spec", None)
+    if spec is None or int(spec[0]) != M.LOCAL_STRIDED:
+        return None
+    w, s = int(spec[1]), int(spec[2])
+    name, stride = select_class_a(mask, N, BQ, A)
+    single = (name, stride, costs(mask, N, BQ, A)[name])
+    parts = []
+    for part in (M.SlidingWindow(w), M.FarStrided(w, s)):
+        pc = costs(part, N, BQ, A)
+        pname, pstride = select_class_a(part, N, BQ, A)
+        parts.append((part, pname, pstride, pc[pname] if pc else None))
+    total = sum(p[3] for p in parts) if all(p[3] is not None for p in parts) else None
+    split = total is not None and total < (1.0 - SPLIT_MARGIN) * single[2]
+    return {"single": single, "parts": parts, "split": split}
+
+
+class SplitChoice:
+    """What ``prepare(..., allow_split=True)`` built for a band + lattice union:
+    the parts with their bases and the ``split.SplitPlan``.  ``run(q, k, v)`` takes
+    and returns tensors in original row order."""
+
+    def __init__(self, mask, N, BQ, A, choice, plan):
+        self.mask, self.N, self.BQ, self.A = mask, N, BQ, A
+        self.name = "split: " + " + ".join(f"{p[0].name} [{p[1]}]" for p in choice["parts"])
+        self.choice, self.plan = choice, plan
+
+    def run(self, q, k, v, scale=None, return_lse=True):
+        o, lse = self.plan.run(q, k, v, scale=scale)
+        return (o, lse) if return_lse else o
+
+
+def prepare(mask, N, BQ, A, device="cuda", allow_split=False):
     """Choose the executable basis with ``select_class_a`` and build, on the GPU,
-    the block index of the mask in that basis and the forward's work list."""
+    the block index of the mask in that basis and the forward's work list.  With
+    ``allow_split``, a band + lattice union that ``select_split`` finds cheaper as
+    a split is built as one instead (the window part on the 64-row kernel, which
+    suits its partial tiles)."""
     from . import attention, blockindex, permute
+    if allow_split:
+        choice = select_split(mask, N, BQ, A)
+        if choice is not None and choice["split"]:
+            from . import split
+            parts = [split.SplitPart(pm, BQ, A, pstride, 64 if i == 0 else 0)
+                     for i, (pm, _, pstride, _) in enumerate(choice["parts"])]
+            return SplitChoice(mask, N, BQ, A, choice, split.SplitPlan(parts, N, device))
     name, stride = select_class_a(mask, N, BQ, A)
     perm = permute.residue_perm_device(N, stride, device) if stride else None
     index = blockindex.build_device(mask, N, BQ, A, perm_q=perm, perm_kv=perm, device=device)

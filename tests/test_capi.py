@@ -105,7 +105,10 @@ def test_argument_errors_before_launch(lib):
     assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20,
                            None) == _lib.PA_ERR_UNSUPPORTED
     assert b"multiple of its row stride" in lib.pa_last_error()
-    a.k_bh_stride, a.perm_kv = 1024 * 128, 20
+    a.k_bh_stride, a.sched_heads = 1024 * 128, -1
+    assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20, None) == _lib.PA_ERR_ARG
+    assert b"sched_heads=-1" in lib.pa_last_error()
+    a.sched_heads, a.perm_kv = 0, 20
     assert lib.pa_attn_fwd(ctypes.byref(a), ctypes.c_void_p(256), 1 << 20, None) == _lib.PA_ERR_ARG
     assert b"16-byte aligned perm_kv" in lib.pa_last_error()
     # merge: null pointers

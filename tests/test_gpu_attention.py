@@ -293,6 +293,24 @@ def test_selector_prepare_end_to_end(name, N, want):
     _assert_close(o, lse, o_ref, lse_ref)
 
 
+@pytest.mark.parametrize("name,N,A", [("local64+str8", 2048, 64), ("local256+str8", 4096, 32)])
+def test_selector_prepare_split_end_to_end(name, N, A):
+    """allow_split: band + lattice unions come back as a split (window part on the
+    64-row kernel, lattice part in its residue basis merging in its epilogue),
+    against the oracle on the union mask."""
+    from polyhedral_b200 import masks, selector
+    m = masks.from_spec(*SPECS[name])
+    sc = selector.prepare(m, N, 128, A, allow_split=True)
+    assert isinstance(sc, selector.SplitChoice), sc
+    assert [p.stride for p in sc.plan.parts] == [0, 8]
+    q, k, v = _rand(2, N, 128, torch.bfloat16, seed=N + A)
+    o, lse = sc.run(q, k, v)
+    o_ref, lse_ref = _oracle(q, k, v, name, N)
+    _assert_close(o, lse, o_ref, lse_ref)
+    # without allow_split the same call keeps the single class A basis
+    assert not isinstance(selector.prepare(m, N, 128, A), selector.SplitChoice)
+
+
 @pytest.mark.parametrize("name,N", [("dilated-4", 8192), ("local64+str8", 16384),
                                     ("window-128", 1024), ("local256+str8", 4096)])
 def test_selector_device_costs_equal_closed_form(name, N):
@@ -309,3 +327,15 @@ def test_selector_device_costs_equal_closed_form(name, N):
     sk = masks.SinksWindow(4, 512)
     assert selector.costs(sk, 8192, 128, 32) is None
     assert selector.costs_device(sk, 8192, 128, 32)["identity"] == 5320704
+
+
+@pytest.mark.parametrize("kv_rows", [0, 64])
+def test_sched_heads_groups_give_identical_results(kv_rows):
+    """Scheduling the work items in head groups (sched_heads) changes the order of
+    the items only: every output bit is the same, ragged last group included."""
+    N, BH = 2048, 5
+    q, k, v = _rand(BH, N, 128, torch.bfloat16, seed=77)
+    ref = _run(q, k, v, "local256+str8", N, 128, 32, kv_rows=kv_rows)
+    for g in (1, 2, 3, BH, 64):
+        o, lse = _run(q, k, v, "local256+str8", N, 128, 32, kv_rows=kv_rows, sched_heads=g)
+        assert torch.equal(o, ref[0]) and torch.equal(lse, ref[1]), g

@@ -82,3 +82,37 @@ def test_select_class_a_configs():
     assert sa(masks_gpu.numpy_mask("local64+str8"), 16384, 128, 32) == ("residue-perm-8", 8)
     assert sa(masks_gpu.numpy_mask("sinks4+win512"), 8192, 128, 32) == ("identity", 0)
     assert sa(masks.FarStrided(1024, 16), 32768, 128, 32)[1] == 16
+
+
+def test_select_split_configs():
+    """Band + lattice unions of configurations 3 and 5: the split into the band
+    (identity) and the lattice beyond it (its residue basis) computes far fewer
+    tiles than any single executable basis."""
+    c3 = selector.select_split(masks_gpu.numpy_mask("local64+str8"), 16384, 128, 64)
+    assert c3["split"] and c3["single"][:2] == ("residue-perm-8", 8)
+    assert [(p[0].name, p[1], p[2]) for p in c3["parts"]] == [
+        ("window-64", "identity", 0), ("far64+str8", "residue-perm-8", 8)]
+    assert sum(p[3] for p in c3["parts"]) < 0.6 * c3["single"][2]
+    c5 = selector.select_split(masks_gpu.numpy_mask("local1024+str16"), 32768, 128, 64)
+    assert c5["split"] and c5["parts"][1][1:3] == ("residue-perm-16", 16)
+    assert selector.select_split(masks.Dilated(4), 1024, 128, 32) is None
+    assert selector.select_split(masks_gpu.numpy_mask("sinks4+win512"), 1024, 128, 32) is None
+
+
+def test_select_split_part_costs_equal_tilings():
+    """Each part's cost is the tiling of that part in its basis, brute force."""
+    from polyhedral_b200 import permute
+    N = 1024
+    for (w, s), (BQ, A) in itertools.product([(64, 8), (16, 4), (100, 8)],
+                                             [(128, 32), (16, 16), (64, 64)]):
+        c = selector.select_split(masks.LocalStrided(w, s), N, BQ, A)
+        assert c["single"][2] == selector.costs(masks.LocalStrided(w, s), N, BQ, A)[c["single"][0]]
+        for part, name, stride, elems in c["parts"]:
+            M = part.dense(N)
+            if stride:
+                p = permute.residue_perm(N, stride)
+                M = M[np.ix_(p, p)]
+            tiles = M.reshape(N // BQ, BQ, N // A, A).any(axis=(1, 3)).sum()
+            assert elems == tiles * BQ * A, (w, s, BQ, A, part.name)
+        live = sum(int(p[0].dense(N).sum()) for p in c["parts"])
+        assert live == int(masks.LocalStrided(w, s).dense(N).sum())
