@@ -55,9 +55,11 @@ WORKLOADS = {
            "c5: window-1024 (identity, 128x128) + far1024+str16 (residue-perm-16, 128x64) "
            "split, LSE merge fused into the second part's epilogue, B2 H64 N32768 D128 bf16"),
 }
-# KV rows per super-tile of the attention kernel, per workload (default 128); the
-# 64-row kernel wins where many tiles are partial (lattice and sinks masks)
-KV_ROWS = {"c3-rp8": 64, "c4": 64}
+# Attention kernel options per workload (``kv_rows``: KV rows per super-tile, 64 =
+# S double-buffered; ``row_threads``: softmax threads per query row), chosen by
+# interleaved measurement; the default kernel elsewhere.
+KERNEL_OPTS = {"c2": {"row_threads": 2}, "c3-rp8": {"row_threads": 2},
+               "c4": {"row_threads": 2}}
 # Workloads computed as a disjoint split, part by part: (mask spec name, BQ, A,
 # residue stride, KV rows per super-tile).  The first part writes O / LSE, the
 # second merges into them in its epilogue.  Band + lattice unions split into the
@@ -65,8 +67,8 @@ KV_ROWS = {"c3-rp8": 64, "c4": 64}
 # each is dense; in one residue basis the band is spread over every off-diagonal
 # block (c3: 2x the tiles).
 SPLITS = {
-    "c3": [("window-64", 128, 64, 0, 64), ("far64+str8", 128, 64, 8, 0)],
-    "c5": [("window-1024", 128, 128, 0, 0), ("far1024+str16", 128, 64, 16, 0)],
+    "c3": [("window-64", 128, 64, 0, {"kv_rows": 64}), ("far64+str8", 128, 64, 8, {})],
+    "c5": [("window-1024", 128, 128, 0, {}), ("far1024+str16", 128, 64, 16, {})],
 }
 
 
@@ -175,12 +177,11 @@ def live_flops(B, H, N, D, name):
 class Pipeline:
     """Mask-only preprocessing plus the per-batch step of one workload."""
 
-    def __init__(self, wl, device):
+    def __init__(self, wl, device, opts=None):
         import torch
         from polyhedral_b200 import attention, blockindex, masks_gpu, permute, split
         B, H, N, D, name, s, BQ, A, seed, _ = WORKLOADS[wl]
-        # mask-heavy workloads (many partial tiles) run the 64-row super-tile kernel
-        self.kv_rows = KV_ROWS.get(wl, 0)
+        self.opts = dict(KERNEL_OPTS.get(wl, {}) if opts is None else opts)
         self.wl, self.B, self.H, self.N, self.D = wl, B, H, N, D
         self.name, self.s, self.BQ, self.A = name, s, BQ, A
         self.device = device
@@ -189,9 +190,12 @@ class Pipeline:
         t0 = time.perf_counter()
         if wl in SPLITS:
             self.split_names = [pn for pn, *_ in SPLITS[wl]]
-            self.split = split.SplitPlan(
-                [split.SplitPart(masks_gpu.numpy_mask(pn), pbq, pa, ps, pkv)
-                 for pn, pbq, pa, ps, pkv in SPLITS[wl]], N, device)
+            parts = []
+            for i, (pn, pbq, pa, ps, popts) in enumerate(SPLITS[wl]):
+                o = dict(opts) if (i == 0 and opts is not None) else dict(popts)
+                parts.append(split.SplitPart(masks_gpu.numpy_mask(pn), pbq, pa, ps,
+                                             o.get("kv_rows", 0), o.get("row_threads", 0)))
+            self.split = split.SplitPlan(parts, N, device)
             self.perm = None
             self.plan = None
         else:
@@ -205,6 +209,14 @@ class Pipeline:
         torch.cuda.synchronize(device)
         self.index_ms = (time.perf_counter() - t0) * 1e3
 
+    def kernel_desc(self):
+        """Attention kernel options of the step (per part for a split)."""
+        if self.split is not None:
+            return [{"part": n, "kv_rows": p.kv_rows or 128, "row_threads": p.row_threads or 1}
+                    for n, p in zip(self.split_names, self.split.parts)]
+        return {"kv_rows": self.opts.get("kv_rows") or 128,
+                "row_threads": self.opts.get("row_threads") or 1}
+
     def launches_per_step(self):
         if self.split is not None:
             return 2                 # attention (window), attention (lattice, merging)
@@ -216,7 +228,7 @@ class Pipeline:
             return self.split.run(q, k, v, out=o, lse_out=lse)
         return attention.block_sparse_attention(
             q, k, v, None, None, None, *self.spec, self.BQ, self.A, residue_stride=self.s,
-            plan=self.plan, return_lse=True, out=o, lse_out=lse, kv_rows=self.kv_rows)
+            plan=self.plan, return_lse=True, out=o, lse_out=lse, **self.opts)
 
     attn_only = step
 
@@ -234,7 +246,7 @@ def run_ours(args, rank, world, device):
     wl = args.workload
     B, H, N, D, name, s, BQ, A, seed, desc = WORKLOADS[wl]
     flops, live = live_flops(B, H, N, D, name)
-    pipe = Pipeline(wl, device)
+    pipe = Pipeline(wl, device, json.loads(args.kernel_opts) if args.kernel_opts else None)
 
     # inputs rotate over enough buffer sets that each step reads data not in L2
     props = torch.cuda.get_device_properties(device)
@@ -461,6 +473,7 @@ def run_ours(args, rank, world, device):
                        "live_elements_per_head": live, "live_gflop_per_step_per_gpu": round(flops / 1e9, 3),
                        "l2": f"inputs rotated over {nbuf} buffer sets ({nbuf * step_bytes >> 20} MiB >= 2x L2)",
                        "index_ms": round(pipe.index_ms, 3),
+                       "kernel": pipe.kernel_desc(),
                        "step": "attention (O, LSE) over the residue permutation applied on the fly, "
                                "inputs/outputs in original order" if pipe.split is None else
                                f"window part + lattice part (residue-{s} on the fly) merging into "
@@ -566,6 +579,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-opts", default=None,
+                    help='attention kernel options replacing the workload\'s defaults '
+                         '(the first part\'s, for a split), e.g. \'{"row_threads": 2}\'')
     ap.add_argument("--profile", action="store_true",
                     help="short run for ncu: no clock fill, no end-to-end leg, no CPU leg")
     args = ap.parse_args()

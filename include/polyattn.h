@@ -68,7 +68,7 @@ typedef struct pa_pred {
 
 /* Message of the last failed call on this host thread ("" if none). */
 PA_API const char* pa_last_error(void);
-/* ABI revision of this header (6); bumped on any incompatible change. */
+/* ABI revision of this header (7); bumped on any incompatible change. */
 PA_API int pa_abi_version(void);
 
 /* ------------------------------------------------------------ block index
@@ -193,6 +193,11 @@ typedef struct pa_attn_args {
                                         run one after another): 0 or >= BH = one group.
                                         Groups whose K/V fit in L2 cut DRAM re-reads when
                                         all heads' K/V do not. */
+  int32_t row_threads;               /* softmax threads per query row of the forward: 0 or
+                                        1 (one thread takes the row's 128 columns of a
+                                        super-tile), or 2 (two threads, 64 columns each,
+                                        16 softmax warps).  2 cannot be combined with
+                                        merge, kv_rows=64 or gathered K/V. */
 } pa_attn_args;
 
 /* Bytes of device workspace pa_attn_plan / pa_attn_fwd need for these arguments

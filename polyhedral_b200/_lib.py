@@ -41,7 +41,7 @@ class PaAttnArgs(ctypes.Structure):
                 ("pred", PaPred), ("scale", c_f32), ("residue_stride", c_i32),
                 ("merge", c_i32), ("kv_rows", c_i32),
                 ("gather_kv", c_i32), ("gather_mult", c_i32), ("gather_scatter", c_i32),
-                ("sched_heads", c_i32)]
+                ("sched_heads", c_i32), ("row_threads", c_i32)]
 
 
 class PaMergeArgs(ctypes.Structure):
@@ -75,7 +75,7 @@ SIGNATURES = {
     "pa_lse_merge": (ctypes.c_int, [ctypes.POINTER(PaMergeArgs), c_vp]),
 }
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 _lib = None
 

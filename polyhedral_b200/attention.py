@@ -24,8 +24,9 @@ disjoint mask on the same rows and merges this one into them in the epilogue
 faster where many tiles are partial, slower on mostly full tiles; not with
 ``merge``).  ``sched_heads=G`` runs the work items in groups of G heads, one group
 after another (default: all heads in one group); groups whose K/V fit in L2 cut DRAM
-re-reads when all heads' K/V do not.
-``num_warps`` / ``num_stages`` are accepted and ignored.
+re-reads when all heads' K/V do not.  ``row_threads=2`` splits every query row's
+softmax over two threads (64 columns each; not with ``merge``, ``kv_rows=64`` or
+gathered K/V).  ``num_warps`` / ``num_stages`` are accepted and ignored.
 
 The reference's class-B traffic emulation (gpu/triton_attn.py:99-128) keeps its
 meaning: ``gather_kv=True`` takes k and v in ORIGINAL order and reads row j of the
@@ -127,7 +128,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
                            num_warps=4, num_stages=2, *, return_lse=False,
                            o_row_map=None, plan=None, out=None, lse_out=None,
                            check=False, residue_stride=0, merge=False, kv_rows=0,
-                           sched_heads=0):
+                           sched_heads=0, row_threads=0):
     """q, k, v: [BH, N, D] (bf16 or fp16, D in {64, 128}), on one CUDA device.
     Returns o [BH, N, D] (same dtype), or (o, lse) with ``return_lse``."""
     gather_mult = max(int(gather_mult), 1)     # <= 1 reads no extra rows, as the reference
@@ -197,6 +198,7 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     a.gather_mult = gather_mult
     a.gather_scatter = 1 if gather_scatter else 0
     a.sched_heads = int(sched_heads or 0)
+    a.row_threads = int(row_threads or 0)
     ws = plan.workspace
     _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
               _lib.stream_handle(dev))

@@ -25,7 +25,8 @@ SOURCES = ["capi_util.cu", "blockindex.cu", "permute.cu", "merge.cu", "attn.cu",
            "attn_k128.cu", "attn_k128r.cu", "attn_k64.cu", "attn_k64r.cu",
            "attn_k128m.cu", "attn_k128rm.cu", "attn_k64m.cu", "attn_k64rm.cu",
            "attn_db128.cu", "attn_db128r.cu", "attn_db64.cu", "attn_db64r.cu",
-           "attn_k128g.cu", "attn_k64g.cu", "attn_noalloc.cu"]
+           "attn_k128g.cu", "attn_k64g.cu",
+           "attn_k128p.cu", "attn_k128rp.cu", "attn_k64p.cu", "attn_k64rp.cu", "attn_noalloc.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -282,6 +282,11 @@ int check_args(const pa_attn_args* a, const char* who) {
     return fail(PA_ERR_UNSUPPORTED, "%s: kv_rows=64 cannot be combined with merge", who);
   PA_CHECK_ARG(!a->merge || a->lse, "%s: merge needs the LSE of the result in place (lse)", who);
   PA_CHECK_ARG(a->sched_heads >= 0, "%s: sched_heads=%d < 0", who, a->sched_heads);
+  PA_CHECK_ARG(a->row_threads >= 0 && a->row_threads <= 2, "%s: row_threads=%d must be 0, 1 or 2",
+               who, a->row_threads);
+  if (a->row_threads == 2 && (a->merge || a->kv_rows == 64 || a->gather_kv || a->gather_mult > 1))
+    return fail(PA_ERR_UNSUPPORTED, "%s: row_threads=2 cannot be combined with merge, "
+                "kv_rows=64 or gathered K/V", who);
   PA_CHECK_ARG(a->gather_kv == 0 || a->gather_kv == 1, "%s: gather_kv=%d must be 0 or 1", who,
                a->gather_kv);
   PA_CHECK_ARG(a->gather_mult >= 0 && a->gather_mult <= 16,
@@ -389,6 +394,12 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   if (gather)
     rc2 = a->D == 128 ? launch_d128_gather(tq, tk, tv, P, grid, L, bf16, stream)
                       : launch_d64_gather(tq, tk, tv, P, grid, L, bf16, stream);
+  else if (a->row_threads == 2 && a->D == 128)
+    rc2 = rs > 0 ? launch_d128_residue_pairs(tq, tk, tv, P, grid, L, bf16, stream)
+                 : launch_d128_pairs(tq, tk, tv, P, grid, L, bf16, stream);
+  else if (a->row_threads == 2)
+    rc2 = rs > 0 ? launch_d64_residue_pairs(tq, tk, tv, P, grid, L, bf16, stream)
+                 : launch_d64_pairs(tq, tk, tv, P, grid, L, bf16, stream);
   else if (rows64 && a->D == 128)
     rc2 = rs > 0 ? db::launch_d128_residue(tq, tk, tv, P, grid, L, bf16, stream)
                  : db::launch_d128(tq, tk, tv, P, grid, L, bf16, stream);

@@ -1,0 +1,14 @@
+// Instantiations of the attention forward kernel for D = 64 with
+// two softmax threads per row (16 softmax warps).
+#include "attn_kernel.cuh"
+
+namespace pa {
+namespace attn {
+
+int launch_d64_pairs(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P,
+                          int grid, int L, bool bf16, cudaStream_t stream) {
+  return launch_family<64, false, false, false, 2>(tq, tk, tv, P, grid, L, bf16, stream);
+}
+
+}  // namespace attn
+}  // namespace pa

@@ -17,6 +17,21 @@ constexpr int kSoftmaxRegs = 200;  // setmaxnreg split of the 384 x 168 launch r
 constexpr int kOtherRegs = 104;    //   256 x 200 + 128 x 104 = 64512
 constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
+
+// Warp roles of the forward kernel by column groups per row (kCG): with kCG = 1 one
+// softmax thread owns a row of S (8 softmax warps, the constants above); with kCG = 2
+// two threads share it, 64 columns each (16 softmax warps, 640 threads; setmaxnreg
+// split of the 640 x 96 launch registers: 512 x 96 + 128 x 88 = 60416; the split
+// with the fewest spills, ptxas -v).
+template <int kCG>
+struct Roles {
+  static constexpr int kSoftmaxWarps = 8 * kCG;
+  static constexpr int kThreads = kCG == 1 ? 384 : 640;
+  static constexpr int kLoadWarp = kSoftmaxWarps;
+  static constexpr int kMmaWarp = kSoftmaxWarps + 1;
+  static constexpr int kSoftmaxRegs = kCG == 1 ? 200 : 96;
+  static constexpr int kOtherRegs = kCG == 1 ? 104 : 88;
+};
 constexpr int BM = 128;   // query rows per half
 constexpr int BN = 128;   // KV rows per super-tile
 constexpr int kTmemCols = 512;
@@ -89,7 +104,7 @@ struct FwdParams {
   int g_kbh, g_vbh, g_kv, g_mult, g_scatter;
 };
 
-template <int D>
+template <int D, int kCG = 1>
 struct Smem {
   static constexpr int kTileBytes = BM * D * 2;               // one 128-row tile, 16-bit
   static constexpr int kSlots = D == 128 ? 4 : 8;
@@ -98,10 +113,13 @@ struct Smem {
   static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
   // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] drain item_full[2]
   //           item_empty[2] kv_full[S] kv_empty[S]
-  static constexpr int kNumBars = 15 + 2 * kSlots;
+  static constexpr int kNumBars = 15 + 2 * kSlots + (kCG == 2 ? 8 : 0);   // + pair_bar[8]
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
-  static constexpr int kEpiOff = (kMiscOff + 32 + 127) & ~127;   // [8 warps][32 rows][128 B]
-  static constexpr int kBytes = kEpiOff + 8 * 32 * 128;
+  // kCG = 1: epilogue staging [8 warps][32 rows][128 B]; kCG = 2: no staging, and the
+  // row-max / row-sum exchange of the two threads of a row [2 halves][2 bufs][2][128]
+  static constexpr int kEpiOff = (kMiscOff + 32 + 127) & ~127;
+  static constexpr int kXchOff = kEpiOff;
+  static constexpr int kBytes = kEpiOff + (kCG == 1 ? 8 * 32 * 128 : 2 * 2 * 2 * 128 * 4);
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
   // gathered K/V only: the landing place of the extra rows nobody reads (one
   // four-row gather: 4 rows x 128 bytes)
@@ -314,11 +332,14 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-template <int D, int L, bool kBf16, bool kRS, bool kMerge, bool kGather = false>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int L, bool kBf16, bool kRS, bool kMerge, bool kGather = false, int kCG = 1>
+__global__ void __launch_bounds__(Roles<kCG>::kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const FwdParams P) {
-  using SM = Smem<D>;
+  using SM = Smem<D, kCG>;
+  using R = Roles<kCG>;
+  constexpr int kLoadWarp = R::kLoadWarp;
+  constexpr int kMmaWarp = R::kMmaWarp;
   constexpr int S = BN / L;              // segments per super-tile
   constexpr int NS = SM::kSlots;
   constexpr int kChunks = D / 64;        // 128-byte swizzle chunks along D
@@ -339,6 +360,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint64_t* item_empty = bars + 13;
   uint64_t* kv_full = bars + 15;
   uint64_t* kv_empty = bars + 15 + NS;
+  uint64_t* pair_bar = bars + 15 + 2 * NS;   // kCG = 2: [half][lane quarter], 64 arrivals
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
   volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
@@ -352,18 +374,20 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       mbar_init(&q_full[h], 1);
       mbar_init(&q_empty[h], 1);
       mbar_init(&s_full[h], 1);
-      mbar_init(&p_full[h], BM);
+      mbar_init(&p_full[h], BM * kCG);
       mbar_init(&o_full[h], 1);
     }
     mbar_init(drain, 1);
     for (int r = 0; r < 2; ++r) {
       mbar_init(&item_full[r], 1);
-      mbar_init(&item_empty[r], 1 + 8);   // MMA thread + one lane per softmax warp
+      mbar_init(&item_empty[r], 1 + R::kSoftmaxWarps);   // MMA thread + a lane per softmax warp
     }
     for (int s = 0; s < NS; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
+    if constexpr (kCG == 2)
+      for (int b = 0; b < 8; ++b) mbar_init(&pair_bar[b], 64);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -382,8 +406,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   const uint32_t tmem = *s_tmem;
 
 
-  if (warp >= 8) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kOtherRegs));
+  if (warp >= R::kSoftmaxWarps) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(R::kOtherRegs));
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ producer
     // Teardown: let every copy issued into the ring and the Q tiles land before the
@@ -690,7 +714,304 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     }
   }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R::kSoftmaxRegs));
+    if constexpr (kCG == 2) {
+      // ------------------------------------------------------------ softmax + epilogue,
+      // two threads per row: warp w of the 16 handles half h = w / 8, S columns
+      // [64 cg, 64 cg + 64) with cg = (w / 4) % 2, and TMEM lane quarter w % 4.  The two
+      // threads of a row combine their partial row maxima through shared memory and a
+      // 64-thread named barrier once per super-tile (so both make the same rescaling
+      // decisions), keep partial row sums, and each writes its half of the O row.  P
+      // columns [32 cg, 32 cg + 32) of the packed P overwrite S columns 64-127, which the
+      // partner has loaded before the barrier.
+      const int h = warp >> 3;
+      const int cg = (warp >> 2) & 1;
+      const int wq = warp & 3;
+      const int r_in = wq * 32 + lane;
+      const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+      const uint32_t tS = tmem + lane_off + h * 128;
+      const uint32_t tO = tmem + lane_off + 256 + h * D + cg * (D / 2);
+      float* xch = reinterpret_cast<float*>(smem + SM::kXchOff);
+      uint64_t* pbar = &pair_bar[h * 4 + wq];
+      uint32_t xb = 0;      // exchanges so far: buffer and barrier parity
+      // this thread's partial value in, the partner's out; the pair meets on an
+      // mbarrier (64 arrivals) whose wait is bounded like every other wait
+      auto exchange = [&](float mine, bool& ok) -> float {
+        float* base = xch + (h * 2 + (xb & 1)) * 2 * BM + r_in;
+        base[cg * BM] = mine;
+        tc_fence_before();     // this thread's TMEM loads before the partner's P stores
+        mbar_arrive(pbar);
+        ok = mbar_wait(pbar, xb & 1, s_abort, err, DEV_TIMEOUT_S) && ok;
+        tc_fence_after();
+        const float other = base[(cg ^ 1) * BM];
+        ++xb;
+        return other;
+      };
+      uint32_t ts = 0, to = 0;
+      const float c2 = P.scale_log2;
+      uint32_t ring = 0;
+      while (true) {
+        const uint32_t rs = ring & 1;
+        bool got = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM);
+        if (!__all_sync(0xffffffffu, got)) break;
+        const int it = s_item[rs];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&item_empty[rs]);
+        ++ring;
+        if (it < 0) break;
+        int p, bh;
+        item_coords(P, it, p, bh);
+        const int cnt = __ldg(P.pv.pair_cnt + p);
+        const int nsup = num_super<L>(P, cnt);
+        const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
+        const uint2* desc = P.pv.desc + (size_t)p * P.pv.cap;
+        const int row = p * 2 * BM + h * BM + r_in;
+        const bool valid = row < P.N;
+        const int irow = !valid        ? -(1 << 30)
+                         : kRS          ? (row % P.nb) * P.rs + row / P.nb
+                         : P.perm_q    ? __ldg(P.perm_q + row)
+                                       : row;
+        float lse_prev = -INFINITY;
+        if constexpr (kMerge) {
+          if (valid) {
+            const int orw0 = kRS          ? (row % P.nb) * P.rs + row / P.nb
+                             : P.o_row_map ? __ldg(P.o_row_map + row)
+                                           : row;
+            if ((unsigned)orw0 < (unsigned)P.N) {
+              const char* op = static_cast<const char*>(P.o) +
+                               ((long long)bh * P.o_bh_stride + (long long)orw0 * P.o_row_stride) * 2 +
+                               cg * D;
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(op));
+              asm volatile("ld.global.f32 %0, [%1];"
+                           : "=f"(lse_prev)
+                           : "l"(P.lse + (long long)bh * P.lse_bh_stride + orw0));
+            }
+          }
+        }
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int u = 0; u < nsup; ++u) {
+          // live bits of this row for this thread's 64 columns, while S is in flight
+          auto word_bits = [&](int sg, int base, int width) -> uint32_t {
+            int e, sub = 0;
+            if (P.A <= BN) {
+              e = u * S + sg;
+            } else {
+              const int spt = P.A / BN;
+              e = u / spt;
+              sub = u - e * spt;
+            }
+            uint2 d = make_uint2(0u, 0u);
+            if (e < cnt) d = __ldg(desc + e);
+            const int st = (d.y >> (24 + 2 * h)) & 3;
+            uint32_t w = st == 1 ? (width == 32 ? 0xffffffffu : 0xffffu) : 0u;
+            if (st == 2) {
+              const int dj = (int)(d.y & 0xffffu);
+              const int sh = (d.y & (1u << 20)) ? (int)((d.y >> 16) & 15u) : -1;
+              const bool ap = (d.y >> 21) & 1u;
+              const int j0 = (int)d.x + sub * BN * dj;
+              if (!(ap && progression_bits(P.pred, irow - j0, j0, dj, sh, base, L, w))) {
+                const int32_t* cols = P.perm_kv ? P.perm_kv + __ldg(ent + e) * P.A + sub * BN + base
+                                                : nullptr;
+                w = element_bits(P.pred, irow, cols, j0, dj, base, width);
+              }
+              if (width == 16) w &= 0xffffu;
+            }
+            return w;
+          };
+          uint32_t mk[2];
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const int kw = 2 * cg + kk;          // 32-column word of the super-tile
+            if constexpr (L >= 32)
+              mk[kk] = word_bits((kw * 32) / L, (kw * 32) % L, 32);
+            else
+              mk[kk] = word_bits(2 * kw, 0, 16) | (word_bits(2 * kw + 1, 0, 16) << 16);
+          }
+          ok = mbar_wait(&s_full[h], ts & 1, s_abort, err, DEV_TIMEOUT_S);
+          ++ts;
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          tc_fence_after();
+          float s[64];
+          {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tS + 64 * cg, r0);
+            tmem_ld32(tS + 64 * cg + 32, r1);
+            tmem_wait_ld();
+            tmem_regs_ready(r0);
+            tmem_regs_ready(r1);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              s[i] = __uint_as_float(r0[i]);
+              s[32 + i] = __uint_as_float(r1[i]);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            if (mk[k] != 0xffffffffu) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (!((mk[k] >> i) & 1u)) s[k * 32 + i] = -INFINITY;
+            }
+          }
+          float mx;
+          {
+            float m8[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) m8[j] = fmaxf(s[2 * j], s[2 * j + 1]);
+#pragma unroll
+            for (int c = 16; c < 64; c += 16) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) m8[j] = fmax3(m8[j], s[c + 2 * j], s[c + 2 * j + 1]);
+            }
+            mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+          }
+          mx = fmaxf(mx, exchange(mx, ok));
+          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          const float m_tile = mx * c2;
+          const float m_new = fmaxf(m_used, m_tile);
+          const float m_prev = m_used;
+          bool bump = false;
+          float factor = 1.f;
+          if (u == 0) {
+            m_used = m_new;
+          } else if (m_new > m_used + 8.0f) {
+            bump = true;
+            factor = ex2(m_used - m_new);
+            m_used = m_new;
+          }
+          // O holds something once any earlier key was live for the row, whichever
+          // thread's columns it was in: decided on the shared maximum, not on this
+          // thread's partial sum, so both threads of the row rescale together
+          const bool need_o = bump && m_prev != -INFINITY;
+          if (bump) l *= factor;
+          const float msub = m_used == -INFINITY ? 0.f : m_used;
+          float r8[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) r8[j] = 0.f;
+#pragma unroll
+          for (int q4 = 0; q4 < 2; ++q4) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int c = q4 * 32 + 2 * i;
+              float x0, x1;
+              ffma2(x0, x1, s[c], s[c + 1], c2, -msub);
+              const float a = ex2(x0);
+              const float b = ex2(x1);
+              const int j = (2 * i) & 7;
+              fadd2(r8[j], r8[j + 1], a, b);
+              pk[i] = pack2<kBf16>(a, b);
+            }
+            tmem_st16(tS + 64 + 32 * cg + q4 * 16, pk);
+          }
+          l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
+          // O rescale (rare), this thread's half of the row
+          if (__any_sync(0xffffffffu, need_o)) {
+            const float f = need_o ? factor : 1.f;
+#pragma unroll 1
+            for (int k = 0; k < D / 64; ++k) {
+              uint32_t r[32];
+              tmem_ld32(tO + k * 32, r);
+              tmem_wait_ld();
+              tmem_regs_ready(r);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+              tmem_st32(tO + k * 32, r);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_full[h]);
+        }
+        if (!ok) break;
+        // epilogue: the row's sum from both threads, O / l, LSE (written by cg 0)
+        l += exchange(l, ok);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        float inv_l = l > 0.f ? 1.f / l : 0.f;
+        const float lse_v = l > 0.f ? (m_used + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
+        float w_old = 0.f;
+        char* orow = nullptr;
+        if (valid) {
+          const int orw = kRS          ? (row % P.nb) * P.rs + row / P.nb
+                          : P.o_row_map ? __ldg(P.o_row_map + row)
+                                        : row;
+          if ((unsigned)orw < (unsigned)P.N) {
+            orow = static_cast<char*>(P.o) +
+                   ((long long)bh * P.o_bh_stride + (long long)orw * P.o_row_stride) * 2 + cg * D;
+            if (P.lse) {
+              float* lp = P.lse + (long long)bh * P.lse_bh_stride + orw;
+              float lse_out = lse_v;
+              if constexpr (kMerge) {
+                const float lo = lse_prev;
+                const float mm = fmaxf(lo, lse_v);
+                float wa = 0.f, wb = 0.f;
+                if (mm != -INFINITY) {
+                  wa = expf(lo - mm);
+                  wb = expf(lse_v - mm);
+                }
+                const float den = wa + wb;
+                const float inv = den > 0.f ? 1.f / den : 0.f;
+                w_old = wa * inv;
+                inv_l *= wb * inv;
+                lse_out = den > 0.f ? mm + logf(den) : -INFINITY;
+              }
+              if (cg == 0) *lp = lse_out;
+            }
+          }
+        }
+        const bool have_o = nsup > 0;
+        if (have_o) {
+          ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
+          ++to;
+          if (!__all_sync(0xffffffffu, ok)) break;
+          tc_fence_after();
+        }
+        // this thread's D/2 columns of the row, 32 at a time, straight to global memory
+#pragma unroll 1
+        for (int k = 0; k < D / 64; ++k) {
+          uint32_t r[32];
+          if (have_o) {
+            tmem_ld32(tO + k * 32, r);
+            tmem_wait_ld();
+            tmem_regs_ready(r);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+          if (orow) {
+            char* dst = orow + k * 64;
+            uint4 ov[4];
+            if constexpr (kMerge) {
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                             : "=r"(ov[c].x), "=r"(ov[c].y), "=r"(ov[c].z), "=r"(ov[c].w)
+                             : "l"(dst + c * 16));
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t w[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float a = __uint_as_float(r[8 * c + 2 * j]) * inv_l;
+                float b = __uint_as_float(r[8 * c + 2 * j + 1]) * inv_l;
+                if constexpr (kMerge) {
+                  const uint32_t old = j == 0 ? ov[c].x : j == 1 ? ov[c].y : j == 2 ? ov[c].z : ov[c].w;
+                  float oa, ob;
+                  unpack2<kBf16>(old, oa, ob);
+                  a = fmaf(w_old, oa, a);
+                  b = fmaf(w_old, ob, b);
+                }
+                w[j] = pack2<kBf16>(a, b);
+              }
+              *reinterpret_cast<uint4*>(dst + c * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+        if (have_o) tc_fence_before();
+      }
+    } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int h = warp >> 2;              // which half
     const int wq = warp & 3;              // TMEM lane quarter
@@ -1059,6 +1380,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       }
       if (have_o) tc_fence_before();
     }
+    }   // kCG == 1
   }
 
   // ------------------------------------------------------------ teardown
@@ -1094,28 +1416,32 @@ PA_DECLARE_LAUNCH(launch_d64_merge)
 PA_DECLARE_LAUNCH(launch_d64_residue_merge)
 PA_DECLARE_LAUNCH(launch_d128_gather)
 PA_DECLARE_LAUNCH(launch_d64_gather)
+PA_DECLARE_LAUNCH(launch_d128_pairs)
+PA_DECLARE_LAUNCH(launch_d128_residue_pairs)
+PA_DECLARE_LAUNCH(launch_d64_pairs)
+PA_DECLARE_LAUNCH(launch_d64_residue_pairs)
 #undef PA_DECLARE_LAUNCH
 
 // Body of the launchers: pick the instantiation for (L, dtype).
-template <int D, bool kRS, bool kMerge, bool kGather = false>
+template <int D, bool kRS, bool kMerge, bool kGather = false, int kCG = 1>
 int launch_family(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParams& P, int grid,
                   int L, bool bf16, cudaStream_t stream) {
   auto go = [&](auto kernel) -> int {
-    const int smem = kGather ? Smem<D>::kAllocGather : Smem<D>::kAlloc;
+    const int smem = kGather ? Smem<D, kCG>::kAllocGather : Smem<D, kCG>::kAlloc;
     PA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
             "pa_attn_fwd");
-    kernel<<<grid, kThreads, smem, stream>>>(tq, tk, tv, P);
+    kernel<<<grid, Roles<kCG>::kThreads, smem, stream>>>(tq, tk, tv, P);
     return PA_OK;
   };
   switch (L) {
-    case 16: return bf16 ? go(attn_fwd_kernel<D, 16, true, kRS, kMerge, kGather>)
-                         : go(attn_fwd_kernel<D, 16, false, kRS, kMerge, kGather>);
-    case 32: return bf16 ? go(attn_fwd_kernel<D, 32, true, kRS, kMerge, kGather>)
-                         : go(attn_fwd_kernel<D, 32, false, kRS, kMerge, kGather>);
-    case 64: return bf16 ? go(attn_fwd_kernel<D, 64, true, kRS, kMerge, kGather>)
-                         : go(attn_fwd_kernel<D, 64, false, kRS, kMerge, kGather>);
-    default: return bf16 ? go(attn_fwd_kernel<D, 128, true, kRS, kMerge, kGather>)
-                         : go(attn_fwd_kernel<D, 128, false, kRS, kMerge, kGather>);
+    case 16: return bf16 ? go(attn_fwd_kernel<D, 16, true, kRS, kMerge, kGather, kCG>)
+                         : go(attn_fwd_kernel<D, 16, false, kRS, kMerge, kGather, kCG>);
+    case 32: return bf16 ? go(attn_fwd_kernel<D, 32, true, kRS, kMerge, kGather, kCG>)
+                         : go(attn_fwd_kernel<D, 32, false, kRS, kMerge, kGather, kCG>);
+    case 64: return bf16 ? go(attn_fwd_kernel<D, 64, true, kRS, kMerge, kGather, kCG>)
+                         : go(attn_fwd_kernel<D, 64, false, kRS, kMerge, kGather, kCG>);
+    default: return bf16 ? go(attn_fwd_kernel<D, 128, true, kRS, kMerge, kGather, kCG>)
+                         : go(attn_fwd_kernel<D, 128, false, kRS, kMerge, kGather, kCG>);
   }
 }
 

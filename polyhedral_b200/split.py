@@ -31,6 +31,7 @@ class SplitPart:
     A: int
     stride: int = 0         # residue-permutation stride; 0 = identity basis
     kv_rows: int = 0        # attention kernel's KV super-tile (0/128, or 64: first part only)
+    row_threads: int = 0    # softmax threads per query row (2: first part only)
 
 
 class SplitPlan:
@@ -41,9 +42,9 @@ class SplitPlan:
         self.N = N
         self.parts = list(parts)
         self.device = torch.device(device)
-        if any(part.kv_rows == 64 for part in self.parts[1:]):
-            raise ValueError("only the first part can use kv_rows=64: later parts merge "
-                             "in their epilogue, which the 64-row kernel does not")
+        if any(part.kv_rows == 64 or part.row_threads == 2 for part in self.parts[1:]):
+            raise ValueError("only the first part can use kv_rows=64 or row_threads=2: later "
+                             "parts merge in their epilogue, which those kernels do not")
         self.perms, self.indices, self.plans = [], [], []
         for part in self.parts:
             perm = None
@@ -70,7 +71,8 @@ class SplitPlan:
             attention.block_sparse_attention(
                 q, k, v, None, None, None, kind, p0, p1, p2, part.BQ, part.A,
                 scale=scale, residue_stride=part.stride, plan=self.plans[i], return_lse=True,
-                out=o, lse_out=lse, merge=i > 0, kv_rows=part.kv_rows)
+                out=o, lse_out=lse, merge=i > 0, kv_rows=part.kv_rows,
+                row_threads=part.row_threads)
         return o, lse
 
     def run_part(self, i, q, k, v, o, lse, scale=None):
@@ -80,7 +82,7 @@ class SplitPlan:
         return attention.block_sparse_attention(
             q, k, v, None, None, None, kind, p0, p1, p2, part.BQ, part.A, scale=scale,
             residue_stride=part.stride, plan=self.plans[i], return_lse=True, out=o,
-            lse_out=lse, merge=i > 0, kv_rows=part.kv_rows)
+            lse_out=lse, merge=i > 0, kv_rows=part.kv_rows, row_threads=part.row_threads)
 
     def live_count(self):
         return sum(int(p.mask.live_count(self.N)) for p in self.parts)
