@@ -60,7 +60,7 @@ def test_split_equals_union_attention():
         assert (lse.cpu() - lse_ref).abs().max().item() < 2e-2
 
 
-@pytest.mark.parametrize("A1,kv1,A2", [(64, 64, 64), (32, 64, 128), (16, 0, 32)])
+@pytest.mark.parametrize("A1,kv1,A2", [(64, 64, 64), (32, 64, 128), (16, 0, 32), (64, "rt2", 64)])
 def test_band_lattice_split_equals_union(A1, kv1, A2):
     """Configuration 3's split: window-64 (identity; the 64-row kernel writes O/LSE)
     + far64+str8 (residue-8 applied by the kernel, merging in its epilogue) equals
@@ -69,7 +69,11 @@ def test_band_lattice_split_equals_union(A1, kv1, A2):
     N, D, BH = 2048, 128, 2
     g = torch.Generator().manual_seed(13)
     q, k, v = (torch.randn(BH, N, D, generator=g).bfloat16().cuda() for _ in range(3))
-    sp = split.local_strided_split(64, 8, N, BQ=128, A=A2, A_window=A1, window_kv_rows=kv1)
+    if kv1 == "rt2":     # window part with two softmax threads per row
+        sp = split.SplitPlan([split.SplitPart(masks.SlidingWindow(64), 128, A1, 0, 0, 2),
+                              split.SplitPart(masks.FarStrided(64, 8), 128, A2, 8)], N)
+    else:
+        sp = split.local_strided_split(64, 8, N, BQ=128, A=A2, A_window=A1, window_kv_rows=kv1)
     o, lse = sp.run(q, k, v)
     M = torch.from_numpy(O.dense_mask(O.LOCAL_STRIDED, 64, 8, 0, N))
     o_ref, lse_ref = O.attention_heads(q.float().cpu(), k.float().cpu(), v.float().cpu(), M)
