@@ -326,48 +326,6 @@ __device__ __forceinline__ void fadd2(float& a0, float& a1, float b0, float b1) 
       "mov.b64 {%0, %1}, ra;\n\t}"
       : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
 }
-// 2^x of two values on the FMA and integer pipes instead of the special-function
-// unit (Cody-Waite reduction x = j + f, j = floor(x), f in [0, 1): adding 1.5 * 2^23
-// rounded toward minus infinity leaves j in the low mantissa bits; 2^f = 1 + f (c1 +
-// c2 f + c3 f^2) with c fitted in the relative least-squares sense on 2000 Chebyshev
-// nodes of [0, 1), max relative error 8.7e-5; j is added to the exponent field).  x
-// is clamped at -127: there f = 0, the polynomial is exactly 1 and the result exactly
-// +0, so masked (-inf) scores give 0 as with ex2.
-__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
-  x0 = fmaxf(x0, -127.f);
-  x1 = fmaxf(x1, -127.f);
-  uint32_t t0, t1, p0, p1;
-  asm("{\n\t.reg .b64 rx, rt, rj, rf, rp, rm, rn, rk, r1, r2, r3;\n\t"
-      "mov.b64 rx, {%4, %5};\n\t"
-      "mov.b64 rm, {%6, %6};\n\t"
-      "mov.b64 rn, {%7, %7};\n\t"
-      "mov.b64 rk, {%8, %8};\n\t"
-      "add.rm.f32x2 rt, rx, rm;\n\t"          // t = x + M rounded down
-      "add.rn.f32x2 rj, rt, rn;\n\t"          // j = t - M (exact)
-      "fma.rn.f32x2 rf, rj, rk, rx;\n\t"      // f = x - j
-      "mov.b64 r1, {%9, %9};\n\t"
-      "mov.b64 r2, {%10, %10};\n\t"
-      "fma.rn.f32x2 rp, r1, rf, r2;\n\t"      // c3 f + c2
-      "mov.b64 r3, {%11, %11};\n\t"
-      "fma.rn.f32x2 rp, rp, rf, r3;\n\t"      // (.) f + c1
-      "mov.b64 r1, {%12, %12};\n\t"
-      "fma.rn.f32x2 rp, rp, rf, r1;\n\t"      // (.) f + c0
-      "mov.b64 {%0, %1}, rt;\n\t"
-      "mov.b64 {%2, %3}, rp;\n\t}"
-      : "=r"(t0), "=r"(t1), "=r"(p0), "=r"(p1)
-      : "f"(x0), "f"(x1), "f"(12582912.0f), "f"(-12582912.0f), "f"(-1.0f),
-        "f"(0.07705804705619812f), "f"(0.22764557600021362f), "f"(0.6951228976249695f),
-        "f"(1.0f));
-  y0 = __uint_as_float(p0 + (t0 << 23));
-  y1 = __uint_as_float(p1 + (t1 << 23));
-}
-
-#ifndef PA_POLY_EVERY
-#define PA_POLY_EVERY 0
-#endif
-// kCG = 2 softmax: every kPolyEvery-th pair of exponentials goes to ex2_poly2 (0: none)
-constexpr int kPolyEvery = PA_POLY_EVERY;
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -939,13 +897,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
               const int c = q4 * 32 + 2 * i;
               float x0, x1;
               ffma2(x0, x1, s[c], s[c + 1], c2, -msub);
-              float a, b;
-              if (kPolyEvery > 0 && i % (kPolyEvery > 0 ? kPolyEvery : 1) == 0) {
-                ex2_poly2(x0, x1, a, b);
-              } else {
-                a = ex2(x0);
-                b = ex2(x1);
-              }
+              const float a = ex2(x0);
+              const float b = ex2(x1);
               const int j = (2 * i) & 7;
               fadd2(r8[j], r8[j + 1], a, b);
               pk[i] = pack2<kBf16>(a, b);
