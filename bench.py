@@ -47,10 +47,10 @@ WORKLOADS = {
            "(residue-perm-8, 128x64) split, LSE merge fused into the second part's epilogue, "
            "B2 H16 N16384 D128 bf16"),
     "c3-rp8": (2, 16, 16384, 128, "local64+str8", 8, 128, 32, 2,
-               "c3 in one basis: local64+str8 + residue-perm-8, 128x32 tiles, 64-row KV "
-               "super-tiles, B2 H16 N16384 D128 bf16"),
+               "c3 in one basis: local64+str8 + residue-perm-8, 128x32 tiles, "
+               "B2 H16 N16384 D128 bf16"),
     "c4": (4, 32, 8192, 128, "sinks4+win512", 0, 128, 32, 3,
-           "c4: sinks4+win512, 128x32 tiles, 64-row KV super-tiles, B4 H32 N8192 D128 bf16"),
+           "c4: sinks4+win512, 128x32 tiles, B4 H32 N8192 D128 bf16"),
     "c5": (2, 64, 32768, 128, "local1024+str16", 16, 128, 64, 4,
            "c5: window-1024 (identity, 128x128) + far1024+str16 (residue-perm-16, 128x64) "
            "split, LSE merge fused into the second part's epilogue, B2 H64 N32768 D128 bf16"),

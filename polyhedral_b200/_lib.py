@@ -120,6 +120,18 @@ def call(name, *args):
 
 
 def stream_handle(device=None):
-    """Raw cudaStream_t of torch's current stream on `device`."""
+    """Raw cudaStream_t of torch's current stream on `device`.  Read through torch's
+    raw-stream accessor when it has one (no Stream object is built per call, which
+    is most of a small call's host time), else through ``current_stream``."""
     import torch
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, int):
+        idx = device
+    else:
+        device = torch.device(device)
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return ctypes.c_void_p(raw(idx))
+    return ctypes.c_void_p(torch.cuda.current_stream(idx).cuda_stream)

@@ -339,3 +339,20 @@ def test_sched_heads_groups_give_identical_results(kv_rows):
     for g in (1, 2, 3, BH, 64):
         o, lse = _run(q, k, v, "local256+str8", N, 128, 32, kv_rows=kv_rows, sched_heads=g)
         assert torch.equal(o, ref[0]) and torch.equal(lse, ref[1]), g
+
+
+def test_stream_handle_follows_current_stream():
+    """Every launch goes to torch's current stream, also inside a stream context and
+    for every way of naming the device."""
+    from polyhedral_b200 import _lib
+    dev = torch.device("cuda:0")
+    assert _lib.stream_handle().value == torch.cuda.current_stream().cuda_stream
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for d in (None, 0, dev, torch.device("cuda"), "cuda:0"):
+            assert _lib.stream_handle(d).value == s.cuda_stream, d
+        q, k, v = _rand(1, 1024, 128, torch.bfloat16, seed=3)
+        o, lse = _run(q, k, v, "causal", 1024, 128, 32)
+    torch.cuda.synchronize()
+    o_ref, lse_ref = _oracle(q, k, v, "causal", 1024)
+    _assert_close(o, lse, o_ref, lse_ref)
