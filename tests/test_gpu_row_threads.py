@@ -107,3 +107,15 @@ def test_argument_errors():
     o, lse = _run(q, k, v, "causal", N, 128, 32)
     with pytest.raises(_lib.PolyattnError):
         _run(q, k, v, "causal", N, 128, 32, row_threads=2, merge=True, out=o, lse_out=lse)
+
+
+@pytest.mark.parametrize("name", ["causal", "window-128", "local256+str8"])
+@pytest.mark.parametrize("N,BQ,A", [(1152, 128, 32), (1152, 128, 128), (1088, 64, 64),
+                                    (1040, 16, 16)])
+def test_ragged_sequence(name, N, BQ, A):
+    """N not a multiple of the 256-row work item: the last item's second half (or part
+    of it) lies past the sequence and must not be written."""
+    q, k, v = _rand(2, N, 128, torch.bfloat16, seed=N + A)
+    o, lse = _run(q, k, v, name, N, BQ, A, row_threads=2)
+    o_ref, lse_ref = _oracle(q, k, v, name, N)
+    _assert_close(o, lse, o_ref, lse_ref)
