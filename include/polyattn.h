@@ -193,11 +193,13 @@ typedef struct pa_attn_args {
                                         run one after another): 0 or >= BH = one group.
                                         Groups whose K/V fit in L2 cut DRAM re-reads when
                                         all heads' K/V do not. */
-  int32_t row_threads;               /* softmax threads per query row of the forward: 0 or
-                                        1 (one thread takes the row's 128 columns of a
-                                        super-tile), or 2 (two threads, 64 columns each,
-                                        16 softmax warps).  2 cannot be combined with
-                                        merge, kv_rows=64 or gathered K/V. */
+  int32_t row_threads;               /* softmax threads per query row of the forward: 1
+                                        (one thread takes the row's 128 columns of a
+                                        super-tile), 2 (two threads, 64 columns each, 16
+                                        softmax warps; not with merge, kv_rows=64 or
+                                        gathered K/V), or 0: the library chooses -- 2 when
+                                        A <= 32 or D = 64 and the call allows it, else 1
+                                        (what measured faster on B200). */
 } pa_attn_args;
 
 /* Bytes of device workspace pa_attn_plan / pa_attn_fwd need for these arguments

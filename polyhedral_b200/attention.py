@@ -26,7 +26,8 @@ faster where many tiles are partial, slower on mostly full tiles; not with
 after another (default: all heads in one group); groups whose K/V fit in L2 cut DRAM
 re-reads when all heads' K/V do not.  ``row_threads=2`` splits every query row's
 softmax over two threads (64 columns each; not with ``merge``, ``kv_rows=64`` or
-gathered K/V).  ``num_warps`` / ``num_stages`` are accepted and ignored.
+gathered K/V), ``row_threads=1`` keeps one; the default (0) lets the library choose:
+two for tiles at most 32 columns wide or D = 64, where they measured faster.  ``num_warps`` / ``num_stages`` are accepted and ignored.
 
 The reference's class-B traffic emulation (gpu/triton_attn.py:99-128) keeps its
 meaning: ``gather_kv=True`` takes k and v in ORIGINAL order and reads row j of the

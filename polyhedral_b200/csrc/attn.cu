@@ -237,6 +237,16 @@ int make_tmap(CUtensorMap* m, const void* base, int dtype, int BH, int N, int D,
 // The reference's class-B emulation knobs are set (gather_kv, or a row multiplier).
 bool gathered(const pa_attn_args* a) { return a->gather_kv || a->gather_mult > 1; }
 
+// Softmax threads per query row the forward runs with.  0 chooses: two where they were
+// measured faster -- tiles at most 32 columns wide (several segments per super-tile,
+// so more per-tile mask work to share) or D = 64 -- unless the call needs a kernel
+// that has only one (merge, 64-row super-tiles, gathered K/V); one otherwise.
+int effective_row_threads(const pa_attn_args* a) {
+  if (a->row_threads) return a->row_threads;
+  if (a->merge || a->kv_rows == 64 || gathered(a)) return 1;
+  return (a->A <= 32 || a->D == 64) ? 2 : 1;
+}
+
 // [BH * rows_per_head][D] 16-bit view of K or V for four-row gathers: box = 64 columns
 // x 1 row, 128-byte swizzle; row j of head b is row b * rows_per_head + j.
 int make_tmap_gather(CUtensorMap* m, const void* base, int dtype, int BH, int N, int D,
@@ -394,10 +404,10 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   if (gather)
     rc2 = a->D == 128 ? launch_d128_gather(tq, tk, tv, P, grid, L, bf16, stream)
                       : launch_d64_gather(tq, tk, tv, P, grid, L, bf16, stream);
-  else if (a->row_threads == 2 && a->D == 128)
+  else if (effective_row_threads(a) == 2 && a->D == 128)
     rc2 = rs > 0 ? launch_d128_residue_pairs(tq, tk, tv, P, grid, L, bf16, stream)
                  : launch_d128_pairs(tq, tk, tv, P, grid, L, bf16, stream);
-  else if (a->row_threads == 2)
+  else if (effective_row_threads(a) == 2)
     rc2 = rs > 0 ? launch_d64_residue_pairs(tq, tk, tv, P, grid, L, bf16, stream)
                  : launch_d64_pairs(tq, tk, tv, P, grid, L, bf16, stream);
   else if (rows64 && a->D == 128)

@@ -64,9 +64,11 @@ def test_reference_gate_matrix(name, dtype):
     q, k, v = _rand(BH, N, D, dtype)
     o_ref, lse_ref = _oracle(q, k, v, name, N)
     tol = 3e-3 if dtype == torch.float16 else ATOL
+    # row_threads: the library's choice (two threads per row at D = 64) and one thread
     for BQ, A in TILES:
-        o, lse = _run(q, k, v, name, N, BQ, A)
-        _assert_close(o, lse, o_ref, lse_ref, atol=tol, rtol=RTOL if tol == ATOL else 0)
+        for rt in (0, 1):
+            o, lse = _run(q, k, v, name, N, BQ, A, row_threads=rt)
+            _assert_close(o, lse, o_ref, lse_ref, atol=tol, rtol=RTOL if tol == ATOL else 0)
 
 
 @pytest.mark.parametrize("name,s", [("dilated-4", 4), ("dilated-8", 8), ("local64+str8", 8)])
@@ -181,9 +183,10 @@ def test_running_max_growth(name):
 def test_ragged_and_large_tiles(N, BQ, A):
     q, k, v = _rand(3, N, 128, torch.bfloat16, seed=N)
     for name in ("causal", "sinks4+win256", "local64+str8"):
-        o, lse = _run(q, k, v, name, N, BQ, A)
         o_ref, lse_ref = _oracle(q, k, v, name, N)
-        _assert_close(o, lse, o_ref, lse_ref)
+        for rt in (0, 1):
+            o, lse = _run(q, k, v, name, N, BQ, A, row_threads=rt)
+            _assert_close(o, lse, o_ref, lse_ref)
 
 
 def test_strided_inputs_scale_and_plan_reuse():

@@ -37,7 +37,10 @@ def _setup(name, s, N, BQ, A, BH=2, D=64, dtype=torch.float16, seed=0, perm_np=N
 
 
 def _attn(q, k, v, idx, spec, BQ, A, pi, **kw):
+    # one softmax thread per row, as the gathered kernel, so that the comparisons
+    # below are bit for bit
     from polyhedral_b200.triton_attn import block_sparse_attention
+    kw.setdefault("row_threads", 1)
     return block_sparse_attention(q, k, v, *idx, *spec, BQ, A, perm_q=pi, perm_kv=pi,
                                   return_lse=True, check=True, **kw)
 
@@ -112,7 +115,7 @@ def test_strided_heads_and_identity_perm():
     bi = blockindex.build(masks.from_spec(*spec), N, BQ, A)
     idx = blockindex.to_cuda(bi)
     oc, lc = block_sparse_attention(q, k.contiguous(), v.contiguous(), *idx, *spec, BQ, A,
-                                    return_lse=True, check=True)
+                                    return_lse=True, check=True, row_threads=1)
     og, lg = block_sparse_attention(q, k, v, *idx, *spec, BQ, A, return_lse=True, check=True,
                                     gather_kv=True, gather_mult=2, gather_scatter=True)
     assert torch.equal(og, oc) and torch.equal(lg, lc)
