@@ -37,7 +37,9 @@ read R - 1 more sets of A rows that the result does not use, rows ``row(j) + r*A
 (``gather_scatter=False``) or ``perm_kv[j + r*A]`` (``gather_scatter=True``),
 mod N.  Not with ``residue_stride``, ``merge`` or ``kv_rows=64``.
 """
+import collections
 import ctypes
+import weakref
 
 import torch
 
@@ -106,6 +108,54 @@ def make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=None, residue_stride
                     perm_kv=perm_kv, residue_stride=residue_stride)
 
 
+# Work lists built by calls without ``plan``, kept when ``set_plan_cache(True)``: the
+# reference's drivers call the forward over and over with one block index, and the
+# list depends on that index only.
+_PLAN_CACHE = collections.OrderedDict()
+_PLAN_CACHE_SIZE = 8
+_plan_cache_on = False
+
+
+def set_plan_cache(on):
+    """Reuse the work list of a call without ``plan`` for later calls with the same
+    block-index tensors (the same objects, unmodified by torch since: their version
+    counters), the same perm_kv, N, BQ, A, residue_stride, and the same stream, so that
+    calls on different streams never share a workspace.  Off by default: a write to
+    the index tensors that bypasses torch (another library's kernel, a DLPack alias)
+    would leave a stale list; call ``clear_plan_cache`` after one.  At most
+    ``_PLAN_CACHE_SIZE`` lists are kept.  ``dropin`` turns it on for the reference's
+    driver scripts, which never rewrite their indices."""
+    global _plan_cache_on
+    _plan_cache_on = bool(on)
+    if not on:
+        clear_plan_cache()
+
+
+def clear_plan_cache():
+    _PLAN_CACHE.clear()
+
+
+def _cached_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv, pk, residue_stride, stream):
+    objs = (kv_idx, kv_num, kv_partial, perm_kv)
+    if not all(t is None or isinstance(t, torch.Tensor) for t in objs):
+        return make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=pk,
+                         residue_stride=residue_stride)
+    key = tuple(id(t) for t in objs) + (int(N), int(BQ), int(A), int(residue_stride), stream)
+    vers = tuple(None if t is None else t._version for t in objs)
+    hit = _PLAN_CACHE.get(key)
+    if hit is not None:
+        refs, v, plan = hit
+        if v == vers and all((r() if r is not None else None) is t for r, t in zip(refs, objs)):
+            _PLAN_CACHE.move_to_end(key)
+            return plan
+    plan = make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=pk,
+                     residue_stride=residue_stride)
+    _PLAN_CACHE[key] = (tuple(None if t is None else weakref.ref(t) for t in objs), vers, plan)
+    while len(_PLAN_CACHE) > _PLAN_CACHE_SIZE:
+        _PLAN_CACHE.popitem(last=False)
+    return plan
+
+
 def _index_tensor(t, dtype, device):
     t = torch.as_tensor(t)
     if t.dtype != dtype:
@@ -154,7 +204,11 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     pk = _perm(perm_kv, N, dev) if perm_kv is not None else pq
     rmap = _perm(o_row_map, N, dev)
 
-    if plan is None:
+    if plan is None and _plan_cache_on:
+        plan = _cached_plan(kv_idx, kv_num, kv_partial, N, BQ, A,
+                            perm_kv if perm_kv is not None else perm_q, pk, residue_stride,
+                            _lib.stream_handle(dev).value)
+    elif plan is None:
         plan = make_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv=pk,
                          residue_stride=residue_stride)
     else:

@@ -27,9 +27,14 @@ MODULES = {
 
 
 def install():
-    """Make ``import blockindex`` (etc.) resolve to this package."""
+    """Make ``import blockindex`` (etc.) resolve to this package, and keep the
+    forward's work lists across calls with the same block index
+    (``attention.set_plan_cache``): the drivers call the forward repeatedly with one
+    index and never rewrite it."""
+    from . import attention
     for name, mod in MODULES.items():
         sys.modules[name] = mod
+    attention.set_plan_cache(True)
 
 
 def main(argv=None):

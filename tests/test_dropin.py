@@ -25,6 +25,8 @@ def test_reference_style_imports_resolve_to_this_package(tmp_path):
         assert permute.__name__ == "polyhedral_b200.permute"
         assert block_sparse_attention.__module__ == "polyhedral_b200.attention"
         assert LAUNCH == ((4, 2),)
+        import polyhedral_b200.attention as attention
+        assert attention._plan_cache_on        # the drivers reuse one index per forward
         for name in ("time_ms", "paired_time", "report"):
             assert callable(getattr(bench, name))
         for name in ("build", "to_cuda"):

@@ -360,3 +360,38 @@ def test_stream_handle_follows_current_stream():
     torch.cuda.synchronize()
     o_ref, lse_ref = _oracle(q, k, v, "causal", 1024)
     _assert_close(o, lse, o_ref, lse_ref)
+
+
+def test_plan_cache():
+    """set_plan_cache(True): a call without ``plan`` reuses the work list of an earlier
+    call with the same index tensors (unchanged since) on the same stream; an in-place
+    change of an index tensor, or another stream, builds a new one; the results are
+    those of calls without the cache."""
+    from polyhedral_b200 import attention, blockindex, masks
+    from polyhedral_b200.triton_attn import block_sparse_attention
+    N = 1024
+    q, k, v = _rand(2, N, 128, torch.bfloat16, seed=8)
+    spec = SPECS["window-128"]
+    kvi, kvn, kvp = blockindex.to_cuda(blockindex.build(masks.from_spec(*spec), N, 128, 32))
+    ref = block_sparse_attention(q, k, v, kvi, kvn, kvp, *spec, 128, 32, return_lse=True)
+    attention.set_plan_cache(True)
+    try:
+        for _ in range(3):
+            o, lse = block_sparse_attention(q, k, v, kvi, kvn, kvp, *spec, 128, 32,
+                                            return_lse=True, check=True)
+            assert torch.equal(o, ref[0]) and torch.equal(lse, ref[1])
+        assert len(attention._PLAN_CACHE) == 1
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            o, lse = block_sparse_attention(q, k, v, kvi, kvn, kvp, *spec, 128, 32,
+                                            return_lse=True, check=True)
+        torch.cuda.synchronize()
+        assert torch.equal(o, ref[0]) and len(attention._PLAN_CACHE) == 2
+        kvn.zero_()            # no listed tile for any row: every row dead
+        o, lse = block_sparse_attention(q, k, v, kvi, kvn, kvp, *spec, 128, 32,
+                                        return_lse=True, check=True)
+        assert (o == 0).all() and torch.isneginf(lse).all()
+        assert len(attention._PLAN_CACHE) == 2      # the stale entry was replaced
+    finally:
+        attention.set_plan_cache(False)
+    assert len(attention._PLAN_CACHE) == 0
