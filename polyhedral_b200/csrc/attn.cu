@@ -47,10 +47,42 @@ constexpr int kPlanThreads = 256;
 // cover each 128-row half, with each half's status.  A tile is full for a half
 // when every covering block lists it as full, dead when no covering block lists
 // it, partial otherwise (the predicate then decides element by element).
+// Per listed tile of every pair, the facts the softmax needs to build its live
+// bits without touching the permutation: x = original index j0 of the tile's first
+// column; y = dj (bits 0-15; the original indices are j0 + c*dj when they form a
+// progression), log2(dj) (bits 16-19) when dj is a power of two (bit 20),
+// progression flag (bit 21), and the two halves' status (bits 24-27).
+__device__ void plan_desc_pair(const PlanView& pv, int p, int cnt,
+                               const int32_t* __restrict__ perm_kv, int A, int rs, int nb) {
+  const int32_t* ent = pv.entries + (size_t)p * pv.cap;
+  const uint8_t* sts = pv.status + (size_t)p * pv.cap;
+  uint2* desc = pv.desc + (size_t)p * pv.cap;
+  for (int e = threadIdx.x; e < cnt; e += kPlanThreads) {
+    const int row0 = ent[e] * A;
+    int j0 = row0, dj = 1;
+    bool ap = true;
+    if (rs > 0) {                 // a residue block holds original rows j0, j0 + rs, ...
+      j0 = (row0 % nb) * rs + row0 / nb;
+      dj = rs;
+    } else if (perm_kv) {
+      j0 = perm_kv[row0];
+      dj = A >= 2 ? perm_kv[row0 + 1] - j0 : 1;
+      ap = dj >= 1 && dj <= 0xffff;
+      for (int c = 2; c < A && ap; ++c) ap = perm_kv[row0 + c] == j0 + c * dj;
+      if (!ap) dj = 0;
+    }
+    uint32_t y = (uint32_t)dj & 0xffffu;
+    if (ap && (dj & (dj - 1)) == 0) y |= ((uint32_t)(31 - __clz(dj)) << 16) | (1u << 20);
+    if (ap) y |= 1u << 21;
+    y |= (uint32_t)(sts[e] & 0xf) << 24;
+    desc[e] = make_uint2((uint32_t)j0, y);
+  }
+}
+
 __global__ void __launch_bounds__(kPlanThreads)
 plan_pairs_kernel(const int32_t* __restrict__ kv_idx, const int32_t* __restrict__ kv_num,
                   const int8_t* __restrict__ kv_partial, int kv_stride, int N, int BQ,
-                  PlanView pv) {
+                  PlanView pv, const int32_t* __restrict__ perm_kv, int A, int rs, int nb) {
   extern __shared__ uint8_t cnt[];   // [4][cap]: present h0, full h0, present h1, full h1
   __shared__ int s_warp[kPlanThreads / 32];
   const int cap = pv.cap;
@@ -123,6 +155,8 @@ plan_pairs_kernel(const int32_t* __restrict__ kv_idx, const int32_t* __restrict_
     }
   }
   if (threadIdx.x == 0) pv.pair_cnt[p] = total;
+  __syncthreads();   // this pair's entries and statuses are written
+  plan_desc_pair(pv, p, total, perm_kv, A, rs, nb);
 }
 
 // Longest-first order of the pairs (stable on ties); work item `it` of the forward
@@ -145,39 +179,6 @@ __global__ void plan_order_kernel(PlanView pv) {
   }
 }
 
-// Per listed tile of every pair, the facts the softmax needs to build its live
-// bits without touching the permutation: x = original index j0 of the tile's first
-// column; y = dj (bits 0-15; the original indices are j0 + c*dj when they form a
-// progression), log2(dj) (bits 16-19) when dj is a power of two (bit 20),
-// progression flag (bit 21), and the two halves' status (bits 24-27).
-__global__ void __launch_bounds__(kPlanThreads)
-plan_desc_kernel(PlanView pv, const int32_t* __restrict__ perm_kv, int A, int rs, int nb) {
-  const int p = blockIdx.x;
-  const int cnt = pv.pair_cnt[p];
-  const int32_t* ent = pv.entries + (size_t)p * pv.cap;
-  const uint8_t* sts = pv.status + (size_t)p * pv.cap;
-  uint2* desc = pv.desc + (size_t)p * pv.cap;
-  for (int e = threadIdx.x; e < cnt; e += kPlanThreads) {
-    const int row0 = ent[e] * A;
-    int j0 = row0, dj = 1;
-    bool ap = true;
-    if (rs > 0) {                 // a residue block holds original rows j0, j0 + rs, ...
-      j0 = (row0 % nb) * rs + row0 / nb;
-      dj = rs;
-    } else if (perm_kv) {
-      j0 = perm_kv[row0];
-      dj = A >= 2 ? perm_kv[row0 + 1] - j0 : 1;
-      ap = dj >= 1 && dj <= 0xffff;
-      for (int c = 2; c < A && ap; ++c) ap = perm_kv[row0 + c] == j0 + c * dj;
-      if (!ap) dj = 0;
-    }
-    uint32_t y = (uint32_t)dj & 0xffffu;
-    if (ap && (dj & (dj - 1)) == 0) y |= ((uint32_t)(31 - __clz(dj)) << 16) | (1u << 20);
-    if (ap) y |= 1u << 21;
-    y |= (uint32_t)(sts[e] & 0xf) << 24;
-    desc[e] = make_uint2((uint32_t)j0, y);
-  }
-}
 
 }  // namespace
 
@@ -453,14 +454,13 @@ extern "C" int pa_attn_plan(const pa_attn_args* a, void* ws, size_t ws_bytes,
     PA_CUDA(cudaFuncSetAttribute(plan_pairs_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem), "pa_attn_plan");
   const cudaStream_t s = (cudaStream_t)stream;
+  const int rs = a->residue_stride;
   plan_pairs_kernel<<<pv.npairs, kPlanThreads, smem, s>>>(a->kv_idx, a->kv_num, a->kv_partial,
-                                                         a->kv_stride, a->N, a->BQ, pv);
+                                                         a->kv_stride, a->N, a->BQ, pv,
+                                                         a->perm_kv, a->A, rs,
+                                                         rs > 0 ? a->N / rs : a->N);
   if ((rc = check_launch("pa_attn_plan"))) return rc;
   plan_order_kernel<<<1, 256, 0, s>>>(pv);
-  if ((rc = check_launch("pa_attn_plan"))) return rc;
-  const int rs = a->residue_stride;
-  plan_desc_kernel<<<pv.npairs, kPlanThreads, 0, s>>>(pv, a->perm_kv, a->A, rs,
-                                                       rs > 0 ? a->N / rs : a->N);
   return check_launch("pa_attn_plan");
 }
 
