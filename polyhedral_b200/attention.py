@@ -11,7 +11,8 @@ tcgen05/TMEM one in csrc/attn.cu; there is no other implementation.
 Extensions (keyword-only): ``return_lse`` returns (o, lse) with lse [BH, N] fp32
 (natural log, -inf for a row with no live key); ``o_row_map`` writes row r of the
 result at ``o_row_map[r]`` (pass ``perm_q`` to get O back in original order, fusing
-the inverse permutation); ``plan`` reuses a work list built once by ``make_plan``;
+the inverse permutation); ``plan`` reuses a work list built once by ``make_plan`` (``set_plan_cache(True)``
+keeps the lists of calls without one, keyed on their index tensors and stream);
 ``out`` / ``lse_out`` supply output buffers; ``check`` synchronises and raises if
 the kernel reported a device-side failure; ``residue_stride=s`` takes q, k, v (and
 returns o, lse) in ORIGINAL row order and runs on their residue permutation by s
@@ -27,7 +28,8 @@ after another (default: all heads in one group); groups whose K/V fit in L2 cut 
 re-reads when all heads' K/V do not.  ``row_threads=2`` splits every query row's
 softmax over two threads (64 columns each; not with ``merge``, ``kv_rows=64`` or
 gathered K/V), ``row_threads=1`` keeps one; the default (0) lets the library choose:
-two for tiles at most 32 columns wide or D = 64, where they measured faster.  ``num_warps`` / ``num_stages`` are accepted and ignored.
+two for tiles at most 32 columns wide or D = 64, where they measured faster.
+``num_warps`` / ``num_stages`` are accepted and ignored.
 
 The reference's class-B traffic emulation (gpu/triton_attn.py:99-128) keeps its
 meaning: ``gather_kv=True`` takes k and v in ORIGINAL order and reads row j of the
