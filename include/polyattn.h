@@ -68,7 +68,7 @@ typedef struct pa_pred {
 
 /* Message of the last failed call on this host thread ("" if none). */
 PA_API const char* pa_last_error(void);
-/* ABI revision of this header (7); bumped on any incompatible change. */
+/* ABI revision of this header (8); bumped on any incompatible change. */
 PA_API int pa_abi_version(void);
 
 /* ------------------------------------------------------------ block index
@@ -215,15 +215,31 @@ PA_API int pa_attn_plan(const pa_attn_args* args, void* workspace, size_t worksp
                  pa_stream_t stream);
 
 /* Runs the forward on a workspace prepared by pa_attn_plan.  A device-side
- * failure (a bounded wait that ran out) leaves a nonzero status in the workspace,
- * readable with pa_attn_status. */
+ * failure (a bounded barrier wait that ran out: every wait gives up after 1 s, and
+ * the kernel then stops issuing work, drains its copies and MMAs and frees TMEM)
+ * is recorded in the workspace, readable with pa_attn_status. */
 PA_API int pa_attn_fwd(const pa_attn_args* args, void* workspace, size_t workspace_bytes,
                 pa_stream_t stream);
 
-/* Copies the workspace status word to *status_host, synchronising `stream`.  The word
- * is cleared by pa_attn_plan and stays nonzero after any failed forward on that
- * workspace until the next plan. */
+/* Status of the most recent forward on `workspace`, synchronising `stream`: 0 when it
+ * finished cleanly, else one of the device codes (1 = a wait on a Q tile ran out,
+ * 2 = K/V ring, 3 = S, 4 = P, 5 = O, 6 = teardown drain, 7 = work-item ring), and the
+ * call returns PA_ERR_DEVICE.  Each launch tags what it records with its own epoch, so
+ * a failure of an earlier forward on the same workspace does not show in a later
+ * clean one.  No counterpart in the reference, whose only failure handling is the
+ * Triton launch retry (gpu/triton_attn.py:224-240). */
 PA_API int pa_attn_status(const void* workspace, int32_t* status_host, pa_stream_t stream);
+
+/* Test hook for the failure path above, no counterpart in the reference: runs
+ * pa_attn_fwd with every bounded wait limited to wait_limit_ns (1 us .. 1 s; the MMA
+ * issuer's waits on Q tiles to a quarter of it, so they run out first) and the first
+ * work item of every CTA missing one Q tile (its load is never issued), so the MMA
+ * issuer's wait on that tile runs out.  The kernel records code 1, stops, drains and
+ * frees TMEM; pa_attn_status then reports it.  Outputs are unspecified.  Not for
+ * gathered K/V (gather_kv / gather_mult). */
+PA_API int pa_attn_fwd_withheld(const pa_attn_args* args, void* workspace,
+                                size_t workspace_bytes, int64_t wait_limit_ns,
+                                pa_stream_t stream);
 
 /* pa_attn_plan + pa_attn_fwd without a caller workspace.  No counterpart in the
  * reference: it exists for callers that may not allocate device memory (a host
@@ -233,11 +249,18 @@ PA_API int pa_attn_status(const void* workspace, int32_t* status_host, pa_stream
  * library holds until exit; a request whose work list would not fit (see
  * pa_attn_workspace_size; about N <= 36096 at A = 16, 51200 at A = 32) is rejected
  * with PA_ERR_ARG.
- * The first call on a device looks up that array's device address (do it before
- * any stream capture).  All calls share the array and each rebuilds what it
- * reads; calls that overlap on the GPU race on it and must be ordered by the
- * caller.  Allocates nothing. */
+ * The first call on a device (and the first in a new CUDA context of it, e.g. after
+ * a device reset) looks up that array's device address; make that first call before
+ * any stream capture.  All calls share the array and each rebuilds what it reads;
+ * calls that overlap on the GPU race on it and must be ordered by the caller.  Calls
+ * no cudaMalloc, cudaFree or other allocating routine. */
 PA_API int pa_attn_fwd_noalloc(const pa_attn_args* args, pa_stream_t stream);
+
+/* Status of the most recent pa_attn_fwd_noalloc on the current device (as
+ * pa_attn_status for a caller workspace: 0, or a device code and PA_ERR_DEVICE),
+ * read from the library's array, synchronising `stream`.  No counterpart in the
+ * reference.  Allocates nothing. */
+PA_API int pa_attn_noalloc_status(int32_t* status_host, pa_stream_t stream);
 
 /* ------------------------------------------------------------ LSE merge
  * Attention over a disjoint union M = P1 + P2 from the attentions over P1 and P2

@@ -71,11 +71,13 @@ SIGNATURES = {
     "pa_attn_plan": (ctypes.c_int, [ctypes.POINTER(PaAttnArgs), c_vp, c_sz, c_vp]),
     "pa_attn_fwd": (ctypes.c_int, [ctypes.POINTER(PaAttnArgs), c_vp, c_sz, c_vp]),
     "pa_attn_status": (ctypes.c_int, [c_vp, ctypes.POINTER(c_i32), c_vp]),
+    "pa_attn_fwd_withheld": (ctypes.c_int, [ctypes.POINTER(PaAttnArgs), c_vp, c_sz, c_i64, c_vp]),
     "pa_attn_fwd_noalloc": (ctypes.c_int, [ctypes.POINTER(PaAttnArgs), c_vp]),
+    "pa_attn_noalloc_status": (ctypes.c_int, [ctypes.POINTER(c_i32), c_vp]),
     "pa_lse_merge": (ctypes.c_int, [ctypes.POINTER(PaMergeArgs), c_vp]),
 }
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 _lib = None
 
@@ -109,10 +111,27 @@ def load():
     return lib
 
 
-def call(name, *args):
-    """Call a C-ABI entry point and raise PolyattnError on a nonzero status."""
+def on_device(device):
+    """Context in which `device` is the current CUDA device.  The library launches on
+    the current device, so a call on tensors of another device switches to theirs for
+    its duration (a no-op context when it is current already, the common case)."""
+    import contextlib
+    import torch
+    idx = device if isinstance(device, int) else torch.device(device).index
+    if idx is None or idx == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(idx)
+
+
+def call(name, *args, device=None):
+    """Call a C-ABI entry point and raise PolyattnError on a nonzero status; with
+    `device`, that device is current during the call."""
     lib = load()
-    rc = getattr(lib, name)(*args)
+    if device is None:
+        rc = getattr(lib, name)(*args)
+    else:
+        with on_device(device):
+            rc = getattr(lib, name)(*args)
     if rc != PA_OK:
         msg = lib.pa_last_error().decode(errors="replace")
         raise PolyattnError(name, rc, msg)

@@ -73,14 +73,16 @@ class AttnPlan:
         nbytes = _lib.load().pa_attn_workspace_size(ctypes.byref(a))
         self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
         _lib.call("pa_attn_plan", ctypes.byref(a), self.workspace.data_ptr(), nbytes,
-                  _lib.stream_handle(device))
+                  _lib.stream_handle(self.workspace.device), device=self.workspace.device)
 
     def status(self):
-        """0 if the last forward on this plan finished cleanly (synchronises)."""
+        """Device status of the most recent forward on this plan (synchronises): 0
+        when it finished cleanly, else the code of the bounded wait that ran out."""
         st = _lib.c_i32(0)
         lib = _lib.load()
-        lib.pa_attn_status(self.workspace.data_ptr(), ctypes.byref(st),
-                           _lib.stream_handle(self.workspace.device))
+        with _lib.on_device(self.workspace.device):
+            lib.pa_attn_status(self.workspace.data_ptr(), ctypes.byref(st),
+                               _lib.stream_handle(self.workspace.device))
         return int(st.value)
 
 
@@ -135,6 +137,13 @@ def set_plan_cache(on):
 
 def clear_plan_cache():
     _PLAN_CACHE.clear()
+
+
+def _drop_cached(plan):
+    """Forget a cached work list (after a forward on it reported a device failure,
+    so that the next call builds a fresh one)."""
+    for key in [k for k, (_, _, p) in _PLAN_CACHE.items() if p is plan]:
+        del _PLAN_CACHE[key]
 
 
 def _cached_plan(kv_idx, kv_num, kv_partial, N, BQ, A, perm_kv, pk, residue_stride, stream):
@@ -258,10 +267,11 @@ def block_sparse_attention(q, k, v, kv_idx, kv_num, kv_partial,
     a.row_threads = int(row_threads or 0)
     ws = plan.workspace
     _lib.call("pa_attn_fwd", ctypes.byref(a), ws.data_ptr(), ws.numel(),
-              _lib.stream_handle(dev))
+              _lib.stream_handle(dev), device=dev)
     if check:
         st = plan.status()
         if st:
+            _drop_cached(plan)
             raise _lib.PolyattnError("pa_attn_fwd", _lib.PA_ERR_DEVICE,
                                      f"device status {st} (a bounded wait ran out)")
     return (o, lse) if return_lse else o

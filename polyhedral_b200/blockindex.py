@@ -113,7 +113,7 @@ def build_device(mask, N, BQ, A, perm_q=None, perm_kv=None, device="cuda", strea
                   pq.data_ptr() if pq is not None else None,
                   pk.data_ptr() if pk is not None else None,
                   kv_idx.data_ptr(), nk, kv_num.data_ptr(), kv_partial.data_ptr(),
-                  stats.data_ptr(), s)
+                  stats.data_ptr(), s, device=device)
         keep = (pq, pk)
     else:
         M = np.stack([np.asarray(mask.row_cols(q, N), dtype=bool) for q in range(N)])
@@ -121,7 +121,7 @@ def build_device(mask, N, BQ, A, perm_q=None, perm_kv=None, device="cuda", strea
             M = M[np.asarray(perm_q)][:, np.asarray(perm_kv)]
         Md = torch.from_numpy(M.astype(np.uint8)).to(device)
         _lib.call("pa_block_index_dense", Md.data_ptr(), N, BQ, A, kv_idx.data_ptr(), nk,
-                  kv_num.data_ptr(), kv_partial.data_ptr(), stats.data_ptr(), s)
+                  kv_num.data_ptr(), kv_partial.data_ptr(), stats.data_ptr(), s, device=device)
         keep = (Md,)
     dbi = DeviceBlockIndex(BQ, A, N, kv_idx, kv_num, kv_partial, stats)
     dbi._keepalive = keep   # inputs must outlive the asynchronous kernel

@@ -33,6 +33,7 @@
 // frees TMEM before exiting.
 #include <cuda.h>
 #include <math.h>
+#include <atomic>
 #include <mutex>
 #include "attn_kernel.cuh"
 #include "attn_kernel_db.cuh"
@@ -174,6 +175,7 @@ __global__ void plan_order_kernel(PlanView pv) {
   }
   if (threadIdx.x == 0) {
     *pv.err = 0;   // a new plan starts with a clean status
+    *pv.done = 0;
     pv.sched[0] = 0;
     pv.sched[1] = 0;
   }
@@ -335,7 +337,14 @@ int check_args(const pa_attn_args* a, const char* who) {
   return PA_OK;
 }
 
-int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
+// Epoch of the next forward launch: 24 bits, never 0 (0 is a clean status word).
+uint32_t next_epoch() {
+  static std::atomic<uint32_t> counter{0};
+  return counter.fetch_add(1, std::memory_order_relaxed) % 0xffffffu + 1u;
+}
+
+int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream,
+               uint64_t wait_ns = kWaitLimitNs, int withhold_q = 0) {
   CUtensorMap tq, tk, tv;
   const bool rows64 = a->kv_rows == 64;
   const int bn = rows64 ? db::BN : BN;
@@ -394,6 +403,12 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream) {
   P.g_kv = a->gather_kv;
   P.g_mult = a->gather_mult > 1 ? a->gather_mult : 1;
   P.g_scatter = a->gather_scatter;
+  P.err.word = pv.err;
+  P.err.epoch = next_epoch();
+  P.err.limit_ns = wait_ns;
+  P.err_q = P.err;
+  if (withhold_q) P.err_q.limit_ns = wait_ns / 4;
+  P.withhold_q = withhold_q;
 
   int dev = 0, sms = 148;
   PA_CUDA(cudaGetDevice(&dev), "pa_attn_fwd");
@@ -476,10 +491,43 @@ extern "C" int pa_attn_fwd(const pa_attn_args* a, void* ws, size_t ws_bytes,
   return launch_fwd(a, plan_view(ws, a->N, a->A), (cudaStream_t)stream);
 }
 
+extern "C" int pa_attn_fwd_withheld(const pa_attn_args* a, void* ws, size_t ws_bytes,
+                                    int64_t wait_limit_ns, pa_stream_t stream) {
+  using namespace pa;
+  using namespace pa::attn;
+  int rc = check_args(a, "pa_attn_fwd_withheld");
+  if (rc) return rc;
+  if (gathered(a))
+    return fail(PA_ERR_UNSUPPORTED, "pa_attn_fwd_withheld: not for gathered K/V");
+  PA_CHECK_ARG(wait_limit_ns >= 1000 && wait_limit_ns <= (int64_t)kWaitLimitNs,
+               "pa_attn_fwd_withheld: wait_limit_ns=%lld outside [1 us, 1 s]",
+               (long long)wait_limit_ns);
+  const PlanSizes sz = plan_sizes(a->N, a->A);
+  PA_CHECK_ARG(ws && ws_bytes >= sz.total && aligned(ws, 256),
+               "pa_attn_fwd_withheld: workspace must be 256-byte aligned and >= %zu bytes",
+               sz.total);
+  return launch_fwd(a, plan_view(ws, a->N, a->A), (cudaStream_t)stream,
+                    (uint64_t)wait_limit_ns, 1);
+}
+
+namespace pa {
+namespace attn {
+// Status of the last forward on the workspace at `ws` (device memory), synchronising
+// `stream`: the error word and the epoch of the last launch that finished.
+int read_status(const void* ws, int32_t* status_host, cudaStream_t stream, const char* who) {
+  int32_t words[2] = {0, 0};
+  const char* b = static_cast<const char*>(ws);
+  PA_CUDA(cudaMemcpyAsync(&words[0], b, sizeof(int32_t), cudaMemcpyDeviceToHost, stream), who);
+  PA_CUDA(cudaMemcpyAsync(&words[1], b + 128, sizeof(int32_t), cudaMemcpyDeviceToHost, stream),
+          who);
+  PA_CUDA(cudaStreamSynchronize(stream), who);
+  *status_host = launch_status(words[0], words[1]);
+  return *status_host ? PA_ERR_DEVICE : PA_OK;
+}
+}  // namespace attn
+}  // namespace pa
+
 extern "C" int pa_attn_status(const void* ws, int32_t* status_host, pa_stream_t stream) {
   PA_CHECK_ARG(ws && status_host, "pa_attn_status: null pointer");
-  PA_CUDA(cudaMemcpyAsync(status_host, ws, sizeof(int32_t), cudaMemcpyDeviceToHost,
-                          (cudaStream_t)stream), "pa_attn_status");
-  PA_CUDA(cudaStreamSynchronize((cudaStream_t)stream), "pa_attn_status");
-  return *status_host ? PA_ERR_DEVICE : PA_OK;
+  return pa::attn::read_status(ws, status_host, (cudaStream_t)stream, "pa_attn_status");
 }

@@ -39,8 +39,9 @@ constexpr uint32_t kDrainLimitNs = 200u * 1000u * 1000u;
 
 // ----------------------------------------------------------------- plan layout
 struct PlanView {
-  int32_t* err;        // status word
+  int32_t* err;        // status word: (launch epoch << 8) | DEV_* code of a failed launch
   int32_t* sched;      // [2]: next work item, CTAs finished (reset by the last CTA)
+  int32_t* done;       // epoch of the last launch whose CTAs all finished
   int32_t* pair_cnt;   // [npairs] union entries of pair p
   int32_t* order;      // [npairs] pairs sorted by decreasing entry count
   int32_t* entries;    // [npairs * cap] ascending A-tile ids
@@ -73,12 +74,25 @@ inline PlanSizes plan_sizes(int N, int A) {
 inline PlanView plan_view(void* ws, int N, int A) {
   const PlanSizes s = plan_sizes(N, A);
   char* b = static_cast<char*>(ws);
-  return PlanView{reinterpret_cast<int32_t*>(b), reinterpret_cast<int32_t*>(b + 64),
-                  reinterpret_cast<int32_t*>(b + s.off_cnt),
-                  reinterpret_cast<int32_t*>(b + s.off_order),
-                  reinterpret_cast<int32_t*>(b + s.off_entries),
-                  reinterpret_cast<uint8_t*>(b + s.off_status),
-                  reinterpret_cast<uint2*>(b + s.off_desc), s.cap, s.npairs};
+  PlanView v;
+  v.err = reinterpret_cast<int32_t*>(b);
+  v.sched = reinterpret_cast<int32_t*>(b + 64);
+  v.done = reinterpret_cast<int32_t*>(b + 128);
+  v.pair_cnt = reinterpret_cast<int32_t*>(b + s.off_cnt);
+  v.order = reinterpret_cast<int32_t*>(b + s.off_order);
+  v.entries = reinterpret_cast<int32_t*>(b + s.off_entries);
+  v.status = reinterpret_cast<uint8_t*>(b + s.off_status);
+  v.desc = reinterpret_cast<uint2*>(b + s.off_desc);
+  v.cap = s.cap;
+  v.npairs = s.npairs;
+  return v;
+}
+
+// Status of the last launch on a workspace from its header words: the failure code
+// when the error word carries that launch's epoch, else 0 (the word is older).
+inline int32_t launch_status(int32_t err_word, int32_t done_epoch) {
+  if (err_word == 0) return 0;
+  return ((uint32_t)err_word >> 8) == (uint32_t)done_epoch ? (err_word & 0xff) : 0;
 }
 
 // ------------------------------------------------------------- plan kernels
@@ -102,6 +116,12 @@ struct FwdParams {
   // K/V rows go through perm_kv, the row multiplier of the K reads (1 = none) and
   // whether the extra rows are scattered
   int g_kbh, g_vbh, g_kv, g_mult, g_scatter;
+  ErrSink err;         // status word of the workspace, this launch's 24-bit epoch
+                       // (nonzero) and the limit of every bounded barrier wait
+  ErrSink err_q;       // the same for the MMA issuer's waits on Q tiles; its limit is a
+                       // quarter of the others' under the withheld-Q test hook, so that
+                       // wait is the one that runs out first, deterministically
+  int withhold_q;      // test hook: never load half 0's Q tile of a CTA's first item
 };
 
 template <int D, int kCG = 1>
@@ -367,7 +387,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint8_t* sEpi = smem + SM::kEpiOff;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int32_t* err = P.pv.err;
+  const ErrSink& err = P.err;   // read from the parameter space where used
 
   if (threadIdx.x == 0) {
     for (int h = 0; h < 2; ++h) {
@@ -418,13 +438,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       for (uint32_t s = 0; s < (uint32_t)NS && s < kv_g; ++s) {
         const uint32_t uses = (kv_g - s + NS - 1) / NS;   // loads issued into slot s
         while (!mbar_try_wait(&kv_full[s], (uses - 1) & 1)) {
-          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+          if (globaltimer() - t0 > kDrainLimitNs) { err.record(DEV_TIMEOUT_DRAIN); break; }
         }
       }
       for (int h = 0; h < 2; ++h) {
         if (q_armed[h] == 0) continue;
         while (!mbar_try_wait(&q_full[h], (q_armed[h] - 1) & 1)) {
-          if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+          if (globaltimer() - t0 > kDrainLimitNs) { err.record(DEV_TIMEOUT_DRAIN); break; }
         }
       }
     };
@@ -567,6 +587,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         for (int h = 0; h < 2 && ok; ++h) {
           if (qi > 0) ok = mbar_wait(&q_empty[h], (qi - 1) & 1, s_abort, err, DEV_TIMEOUT_Q);
           if (!ok) break;
+          // test hook (pa_attn_fwd_withheld): the first item's half-0 Q tile is never
+          // loaded, so the MMA warp's bounded wait on it runs out
+          if (qi == 0 && h == 0 && P.withhold_q) continue;
           mbar_arrive_expect_tx(&q_full[h], SM::kTileBytes);
           ++q_armed[h];
           const int qr = p * 2 * BM + h * BM;
@@ -670,8 +693,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         item_coords(P, it, p, bh_unused);
         const int nsup = num_super<L>(P, __ldg(P.pv.pair_cnt + p));
         if (nsup == 0) continue;
-        ok = mbar_wait(&q_full[0], qi & 1, s_abort, err, DEV_TIMEOUT_Q) &&
-             mbar_wait(&q_full[1], qi & 1, s_abort, err, DEV_TIMEOUT_Q);
+        ok = mbar_wait(&q_full[0], qi & 1, s_abort, P.err_q, DEV_TIMEOUT_Q) &&
+             mbar_wait(&q_full[1], qi & 1, s_abort, P.err_q, DEV_TIMEOUT_Q);
         tc_fence_after();
         if (!ok) break;
         uint32_t ks, vs;
@@ -709,7 +732,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       tc_commit(drain);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(drain, 0)) {
-        if (globaltimer() - t0 > kDrainLimitNs) { atomicCAS(err, 0, DEV_TIMEOUT_DRAIN); break; }
+        if (globaltimer() - t0 > kDrainLimitNs) { err.record(DEV_TIMEOUT_DRAIN); break; }
       }
     }
   }
@@ -1395,6 +1418,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     if (atomicAdd(P.pv.sched + 1, 1) == (int)gridDim.x - 1) {
       atomicExch(P.pv.sched, 0);
       atomicExch(P.pv.sched + 1, 0);
+      atomicExch(P.pv.done, (int32_t)P.err.epoch);   // every CTA has recorded its status
     }
   }
 }

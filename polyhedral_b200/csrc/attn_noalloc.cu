@@ -16,6 +16,8 @@
 // everything in it that the kernels read, so nothing carries over between calls;
 // two calls whose work overlaps on the GPU (different streams, or several host
 // threads without ordering) race on the array and must not be issued.
+// pa_attn_noalloc_status reads the device status the last call left in the array.
+#include <cuda.h>
 #include <mutex>
 #include "capi_util.h"
 #include "common.cuh"
@@ -28,23 +30,50 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_attn_scratch[kNoAllocScratchBytes];
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  });
+  return fn;
+}
+
+// Device address of g_attn_scratch, per device and per CUDA context: the host-side
+// name is only a stand-in for the symbol, and a context created after a device
+// reset loads the module afresh, possibly at another address.
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of g_attn_scratch on the current device, looked up once per
-// device (the host-side name is only a stand-in for the symbol).
-int scratch_for_current_device(void** out) {
+int scratch_for_current_device(void** out, const char* who) {
   int dev = 0;
-  PA_CUDA(cudaGetDevice(&dev), "pa_attn_fwd_noalloc");
+  PA_CUDA(cudaGetDevice(&dev), who);
   if (dev < 0 || dev >= kMaxDevices)
-    return fail(PA_ERR_UNSUPPORTED, "pa_attn_fwd_noalloc: device %d beyond %d", dev, kMaxDevices);
+    return fail(PA_ERR_UNSUPPORTED, "%s: device %d beyond %d", who, dev, kMaxDevices);
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get) return fail(PA_ERR_CUDA, "%s: cuCtxGetCurrent unavailable", who);
+  CUcontext ctx = nullptr;   // NULL until the runtime binds a context to this thread
+  if (get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
-    PA_CUDA(cudaGetSymbolAddress(&p, g_attn_scratch), "pa_attn_fwd_noalloc: cudaGetSymbolAddress");
-    g_scratch_ptr[dev] = p;
+  if (ctx && g_scratch_ptr[dev] && g_scratch_ctx[dev] == ctx) {
+    *out = g_scratch_ptr[dev];
+    return PA_OK;
   }
-  *out = g_scratch_ptr[dev];
+  // the lookup binds the device's primary context to this thread if none was
+  void* p = nullptr;
+  PA_CUDA(cudaGetSymbolAddress(&p, g_attn_scratch), who);
+  if (get(&ctx) != CUDA_SUCCESS || !ctx)
+    return fail(PA_ERR_CUDA, "%s: no current CUDA context after the symbol lookup", who);
+  g_scratch_ptr[dev] = p;
+  g_scratch_ctx[dev] = ctx;
+  *out = p;
   return PA_OK;
 }
 
@@ -62,9 +91,18 @@ extern "C" int pa_attn_fwd_noalloc(const pa_attn_args* args, pa_stream_t stream)
                 "scratch (N=%d, A=%d); use pa_attn_plan/pa_attn_fwd with a caller workspace",
                 need, kNoAllocScratchBytes, args->N, args->A);
   void* ws = nullptr;
-  int rc = scratch_for_current_device(&ws);
+  int rc = scratch_for_current_device(&ws, "pa_attn_fwd_noalloc");
   if (rc) return rc;
   rc = pa_attn_plan(args, ws, kNoAllocScratchBytes, stream);
   if (rc) return rc;
   return pa_attn_fwd(args, ws, kNoAllocScratchBytes, stream);
+}
+
+extern "C" int pa_attn_noalloc_status(int32_t* status_host, pa_stream_t stream) {
+  using namespace pa;
+  PA_CHECK_ARG(status_host != nullptr, "pa_attn_noalloc_status: null status_host");
+  void* ws = nullptr;
+  int rc = scratch_for_current_device(&ws, "pa_attn_noalloc_status");
+  if (rc) return rc;
+  return attn::read_status(ws, status_host, (cudaStream_t)stream, "pa_attn_noalloc_status");
 }

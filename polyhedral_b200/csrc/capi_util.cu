@@ -21,4 +21,4 @@ void clear_error() { g_last_error.clear(); }
 
 extern "C" const char* pa_last_error(void) { return pa::g_last_error.c_str(); }
 
-extern "C" int pa_abi_version(void) { return 7; }
+extern "C" int pa_abi_version(void) { return 8; }

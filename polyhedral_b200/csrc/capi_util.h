@@ -47,4 +47,10 @@ inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }
 
+namespace attn {
+// Status of the last attention forward on a workspace (device memory), read
+// stream-ordered and synchronising `stream` (csrc/attn.cu).
+int read_status(const void* ws, int32_t* status_host, cudaStream_t stream, const char* who);
+}  // namespace attn
+
 }  // namespace pa

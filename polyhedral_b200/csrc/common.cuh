@@ -63,22 +63,38 @@ PA_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
+// Where a kernel launch reports a failure: a status word in global memory, tagged
+// with the launch's epoch (bits 8-31) above the failure code (bits 0-7), so that a
+// word left by an earlier launch on the same workspace reads as stale, not as this
+// launch's status.  Also carries the launch's wait limit.
+struct ErrSink {
+  int32_t* word;
+  uint32_t epoch;      // 24-bit launch epoch
+  uint64_t limit_ns;   // bounded waits give up after this long
+  // Records `code` for this launch.  A wait that gives up raises the CTA's abort
+  // flag, so the CTA's other waits stop without recording: the word holds the
+  // failure of whichever CTA recorded last, a word of an earlier launch is replaced.
+  PA_DEV void record(int32_t code) const {
+    if (word) atomicExch(word, (int32_t)((epoch << 8) | ((uint32_t)code & 0xffu)));
+  }
+};
+
 // Wait for the phase of `bar` with parity `parity` to complete.  Gives up after
-// kWaitLimitNs, or as soon as another thread of the CTA has raised `*abort`;
-// on its own timeout it raises `*abort` and records `code` in `*err` (global).
+// err.limit_ns, or as soon as another thread of the CTA has raised `*abort`;
+// on its own timeout it raises `*abort` and records `code` through `err`.
 // Returns false when it gave up.  try_wait itself blocks in hardware for a
 // system-defined time before returning false; a suspend-time hint (measured)
 // made the attention kernel about 1.5 % slower, so none is given.
 PA_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                      int32_t* err, int32_t code) {
+                      const ErrSink& err, int32_t code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > err.limit_ns) {
       *abort = 1;
-      if (err) atomicCAS(err, 0, code);
+      err.record(code);
       return false;
     }
   }

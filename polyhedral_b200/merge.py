@@ -45,5 +45,5 @@ def lse_merge(o1, lse1, o2, lse2, row_map2=None, out=None, lse_out=None):
     a.lse1_bh_stride, a.lse2_bh_stride, a.lse_bh_stride = (lse1.stride(0), lse2.stride(0),
                                                            lse.stride(0))
     a.row_map2 = rm.data_ptr() if rm is not None else None
-    _lib.call("pa_lse_merge", ctypes.byref(a), _lib.stream_handle(o1.device))
+    _lib.call("pa_lse_merge", ctypes.byref(a), _lib.stream_handle(o1.device), device=o1.device)
     return o, lse

@@ -25,7 +25,8 @@ def identity_perm(N):
 def residue_perm_device(N, s, device="cuda"):
     import torch
     out = torch.empty(N, dtype=torch.int32, device=device)
-    _lib.call("pa_residue_perm", N, s, out.data_ptr(), _lib.stream_handle(out.device))
+    _lib.call("pa_residue_perm", N, s, out.data_ptr(), _lib.stream_handle(out.device),
+              device=out.device)
     return out
 
 
@@ -68,7 +69,7 @@ def _permute(tensors, perm, scatter, outs=None):
                                  src.stride(0) * es, src.stride(1) * es,
                                  dst.stride(0) * es, dst.stride(1) * es)
         _lib.call("pa_permute_rows", arr, len(group), BH, N, D * es, p.data_ptr(),
-                  1 if scatter else 0, s)
+                  1 if scatter else 0, s, device=tensors[0].device)
     return outs
 
 
@@ -97,7 +98,8 @@ def invert(perm):
     N = perm.numel()
     p32 = perm.to(torch.int32).contiguous()
     inv = torch.empty_like(p32)
-    _lib.call("pa_invert_perm", p32.data_ptr(), N, inv.data_ptr(), _lib.stream_handle(perm.device))
+    _lib.call("pa_invert_perm", p32.data_ptr(), N, inv.data_ptr(), _lib.stream_handle(perm.device),
+              device=perm.device)
     return inv.to(perm.dtype)
 
 

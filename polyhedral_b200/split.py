@@ -21,7 +21,7 @@ from typing import Optional
 import numpy as np
 import torch
 
-from . import attention, blockindex, masks, permute
+from . import attention, blockindex, masks, permute, shard
 
 
 @dataclass
@@ -83,6 +83,17 @@ class SplitPlan:
             q, k, v, None, None, None, kind, p0, p1, p2, part.BQ, part.A, scale=scale,
             residue_stride=part.stride, plan=self.plans[i], return_lse=True, out=o,
             lse_out=lse, merge=i > 0, kv_rows=part.kv_rows, row_threads=part.row_threads)
+
+    def run_shard(self, q, k, v, rank, world, scale=None, out=None, lse_out=None):
+        """This rank's share of ``run``: the contiguous (batch, head) range
+        ``shard.shard_bh(BH, rank, world)`` of the full-size q, k, v (views, no copy),
+        with the same plans; returns that range's (o, lse) (rows of out / lse_out
+        when given, full-size).  No collective: ``shard.gather`` assembles the whole
+        result when a caller needs it on one rank."""
+        sh = shard.shard_bh(q.shape[0], rank, world)
+        return sh.run(lambda q_, k_, v_, out, lse_out: self.run(q_, k_, v_, scale=scale, out=out,
+                                                                  lse_out=lse_out),
+                      q, k, v, out=out, lse_out=lse_out)
 
     def live_count(self):
         return sum(int(p.mask.live_count(self.N)) for p in self.parts)

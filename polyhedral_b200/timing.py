@@ -1,77 +1,97 @@
-"""CUDA-event timing with an L2 flush between repetitions (the methodology of
-the reference's ``gpu/bench.py``, :11-74: medians, warm-up, flushed cache, and
-interleaved A/B pairs for comparisons).  The flush buffer is sized from the
-device's L2 (twice its size) rather than a fixed 64 MB."""
+"""Device timing for the reference's driver scripts, under the names they import
+from their ``bench`` module (gpu/bench.py): ``time_ms``, ``paired_time``, ``report``.
+
+Design: one ``_Timer`` owns an L2-sized scrub buffer and times single calls with a
+pair of CUDA events on the current stream, synchronising after each call, so every
+sample is one cold-L2 call.  ``time_ms`` summarises many samples of one callable;
+``paired_time`` interleaves two callables, alternating which of the pair runs first
+so neither always follows the other's cache state, and summarises the per-pair
+ratios.  ``report`` prints a right-aligned fixed-width table.  The scrub buffer is
+twice the device's L2 (126 MB on B200), not a fixed size.
+"""
 import statistics
 
 
-def _flush_buffer(device=None):
-    import torch
-    props = torch.cuda.get_device_properties(device)
-    l2 = getattr(props, "L2_cache_size", 0) or (128 << 20)
-    return torch.empty(2 * l2 // 4, dtype=torch.int32, device=device)
+class _Timer:
+    """Times one call of a callable on the current CUDA stream."""
+
+    def __init__(self, scrub_l2=True):
+        import torch
+        self._torch = torch
+        self._scrub = None
+        if scrub_l2:
+            props = torch.cuda.get_device_properties(torch.cuda.current_device())
+            l2 = getattr(props, "L2_cache_size", 0) or (128 << 20)
+            self._scrub = torch.empty(2 * l2, dtype=torch.uint8, device="cuda")
+        self._ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        self._tick = 0
+
+    def __call__(self, fn):
+        if self._scrub is not None:       # evict the previous call's data from L2
+            self._tick = (self._tick + 1) & 0xFF
+            self._scrub.fill_(self._tick)
+        start, stop = self._ev
+        start.record()
+        fn()
+        stop.record()
+        stop.synchronize()
+        return start.elapsed_time(stop)
+
+
+def _spread(xs):
+    return statistics.stdev(xs) if len(xs) > 1 else 0.0
 
 
 def time_ms(fn, warmup=25, reps=100, flush_l2=True):
-    """Median and stdev (ms) of ``fn()`` over ``reps`` CUDA-event-timed calls on
-    the current stream."""
-    import torch
-    cache = _flush_buffer() if flush_l2 else None
+    """(median, standard deviation) in ms of ``reps`` single calls of ``fn`` after
+    ``warmup`` untimed ones, L2 scrubbed before each timed call."""
+    timer = _Timer(flush_l2)
     for _ in range(warmup):
         fn()
-    torch.cuda.synchronize()
-    out = []
-    for _ in range(reps):
-        if cache is not None:
-            cache.zero_()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        fn()
-        e.record()
-        torch.cuda.synchronize()
-        out.append(s.elapsed_time(e))
-    return statistics.median(out), (statistics.stdev(out) if len(out) > 1 else 0.0)
+    samples = sorted(timer(fn) for _ in range(reps))
+    return statistics.median(samples), _spread(samples)
 
 
 def paired_time(fn_a, fn_b, warmup=25, reps=200, flush_l2=True):
-    """Interleaved timing of two callables; returns (median_a, median_b,
-    median of per-pair b/a ratios, stdev of the ratios)."""
-    import torch
-    cache = _flush_buffer() if flush_l2 else None
+    """Interleaved A/B timing: (median ms of a, median ms of b, median of the
+    per-pair ratios b / a, their standard deviation).  Each pair runs both calls
+    back to back, a first in even pairs and b first in odd ones."""
+    timer = _Timer(flush_l2)
     for _ in range(warmup):
         fn_a()
         fn_b()
-    torch.cuda.synchronize()
-    a_s, b_s, ratios = [], [], []
-    for _ in range(reps):
-        pair = []
-        for fn in (fn_a, fn_b):
-            if cache is not None:
-                cache.zero_()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            fn()
-            e.record()
-            torch.cuda.synchronize()
-            pair.append(s.elapsed_time(e))
-        a_s.append(pair[0])
-        b_s.append(pair[1])
-        if pair[0] > 0:
-            ratios.append(pair[1] / pair[0])
-    return (statistics.median(a_s), statistics.median(b_s), statistics.median(ratios),
-            statistics.stdev(ratios) if len(ratios) > 1 else 0.0)
+    ta, tb = [], []
+    for i in range(reps):
+        if i % 2 == 0:
+            a = timer(fn_a)
+            b = timer(fn_b)
+        else:
+            b = timer(fn_b)
+            a = timer(fn_a)
+        ta.append(a)
+        tb.append(b)
+    ratios = [b / a for a, b in zip(ta, tb) if a > 0]
+    return statistics.median(ta), statistics.median(tb), statistics.median(ratios), _spread(ratios)
+
+
+def _cell(value, width):
+    """One right-aligned table cell: floats with three decimals, integers whole."""
+    if isinstance(value, bool) or not isinstance(value, (int, float)):
+        return format(str(value), f">{width}")
+    if isinstance(value, int):
+        return format(value, f">{width}d")
+    return format(value, f">{width}.3f")
 
 
 def report(rows, cols, title=None, note=None):
-    """Fixed-width table (gpu/bench.py:27-38)."""
+    """Print `rows` as a table whose columns are ``cols = [(header, width), ...]``,
+    under an optional title and its rule, followed by an optional note."""
+    widths = [w for _, w in cols]
+    lines = []
     if title:
-        print(f"\n{title}")
-        print("-" * max(len(title), sum(w for _, w in cols)))
-    print("".join(f"{h:>{w}}" for h, w in cols))
-    for r in rows:
-        print("".join(
-            (f"{v:>{w}.{3 if isinstance(v, float) else 0}f}" if isinstance(v, (int, float))
-             else f"{str(v):>{w}}")
-            for v, (_, w) in zip(r, cols)))
+        lines += ["", title, "-" * max(len(title), sum(widths))]
+    lines.append("".join(_cell(h, w) for h, w in cols))
+    lines += ["".join(_cell(v, w) for v, w in zip(r, widths)) for r in rows]
     if note:
-        print(f"\n{note}")
+        lines += ["", note]
+    print("\n".join(lines))

@@ -126,6 +126,26 @@ def test_fused_merge_matches_union(stride2, BQ, A):
     assert (o == 0).all() and torch.isneginf(lse).all()
 
 
+@pytest.mark.parametrize("w,s,A1,A2", [(1024, 16, 128, 64), (256, 16, 128, 64), (64, 8, 64, 64)])
+def test_c5_shaped_split_rp16_merging(w, s, A1, A2):
+    """Configuration 5's split shapes at N = 4096: the window part at 128 x A1 in the
+    identity basis writes O / LSE, then the far lattice at 128 x 64 in the residue-s
+    basis merges into them in its epilogue; against the union mask."""
+    from polyhedral_b200 import masks
+    N, D, BH = 4096, 128, 2
+    g = torch.Generator().manual_seed(w + s)
+    q, k, v = (torch.randn(BH, N, D, generator=g).bfloat16().cuda() for _ in range(3))
+    p1, p2 = masks.SlidingWindow(w), masks.FarStrided(w, s)
+    o, lse = _part(q, k, v, p1, N, 128, A1)
+    _part(q, k, v, p2, N, 128, A2, s, out=o, lse_out=lse, merge=True)
+    o_ref, lse_ref = _union_ref(q, k, v, p1.dense(N) | p2.dense(N))
+    err = (o.float().cpu() - o_ref).abs()
+    assert (err <= 2e-2 + 1e-2 * o_ref.abs()).all(), err.max()
+    fin = torch.isfinite(lse_ref)
+    assert torch.equal(torch.isfinite(lse.cpu()), fin)
+    assert (lse.cpu()[fin] - lse_ref[fin]).abs().max().item() < 2e-2
+
+
 def test_fused_merge_equals_merge_kernel():
     """The fused merge and attention + pa_lse_merge agree within one bf16 rounding
     (the fused path merges this part's fp32 result before rounding)."""

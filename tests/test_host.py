@@ -80,3 +80,42 @@ def test_flex_mask_mod_far_strided():
     assert bool(M[1024, 0]) and not bool(M[1025, 0]) and bool(M[2047, 2047 - 1024])
     np.testing.assert_array_equal(M.numpy(), masks.FarStrided(1024, 16).dense(2048))
     assert torch.equal(M, masks_gpu.dense_bool("far1024+str16", 2048, device="cpu"))
+
+
+def test_report_table(capsys):
+    """The drivers' table printer: right-aligned cells, floats with three decimals."""
+    from polyhedral_b200 import timing
+    timing.report([("a", 1.23456, 7), ("bb", 10.0, 12)], [("x", 4), ("t", 9), ("n", 5)],
+                  title="T", note="done")
+    out = capsys.readouterr().out.splitlines()
+    assert out[1:3] == ["T", "-" * 18]
+    assert out[3] == "   x        t    n"
+    assert out[4] == "   a    1.235    7"
+    assert out[5] == "  bb   10.000   12"
+    assert out[-1] == "done"
+
+
+def test_on_device_switches_only_for_another_device(monkeypatch):
+    """Library calls run with the tensors' device current: a no-op context when it is
+    current already, torch.cuda.device(index) otherwise."""
+    import contextlib
+    import torch
+    from polyhedral_b200 import _lib
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    assert isinstance(_lib.on_device(torch.device("cuda:0")), contextlib.nullcontext)
+    assert isinstance(_lib.on_device("cuda"), contextlib.nullcontext)
+    ctx = _lib.on_device(torch.device("cuda", 1))
+    assert isinstance(ctx, torch.cuda.device) and ctx.idx == 1
+    assert _lib.on_device(3).idx == 3
+
+
+def test_drop_cached_plan():
+    from polyhedral_b200 import attention
+    a, b = object(), object()
+    attention._PLAN_CACHE.clear()
+    attention._PLAN_CACHE[1] = ((), (), a)
+    attention._PLAN_CACHE[2] = ((), (), b)
+    attention._PLAN_CACHE[3] = ((), (), a)
+    attention._drop_cached(a)
+    assert list(attention._PLAN_CACHE) == [2]
+    attention._PLAN_CACHE.clear()

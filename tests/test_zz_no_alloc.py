@@ -5,10 +5,13 @@ Some users of this library run where they may not allocate GPU memory (inside
 another framework's pool, under a fixed budget, or through a binding with no
 device allocator); the no-alloc entry point keeps its work list in a fixed array
 inside the library instead of a caller workspace.  This test calls both entry
-points through the C ABI on the same inputs and requires the same outputs, twice
-in a row (the shared array keeps the previous call's contents, so the second call
-checks that nothing stale is read).  It lives in its own file named to be
-collected last, and runs alone in a fresh process as well.
+points through the C ABI on the same inputs and requires bit-identical outputs
+(the same kernels run on the same data), reads the no-alloc call's own device
+status from the library's array (pa_attn_noalloc_status), and does so for two
+calls in a row with different masks, sizes and tile shapes: the array keeps the
+first call's contents, so the second call shows that nothing stale is read.  It
+lives in its own file named to be collected last, and runs alone in a fresh
+process as well.
 """
 import ctypes
 
@@ -20,7 +23,7 @@ import oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def _args(q, k, v, o, lse, dbi, spec, perm, BQ, A):
+def _args(q, k, v, o, lse, dbi, spec, s, BQ, A):
     from polyhedral_b200 import _lib
     a = _lib.PaAttnArgs()
     BH, N, D = q.shape
@@ -34,54 +37,60 @@ def _args(q, k, v, o, lse, dbi, spec, perm, BQ, A):
     a.kv_idx, a.kv_num, a.kv_partial = (dbi.kv_idx.data_ptr(), dbi.kv_num.data_ptr(),
                                         dbi.kv_partial.data_ptr())
     a.kv_stride, a.BQ, a.A = dbi.kv_idx.shape[1], BQ, A
-    p = perm.data_ptr() if perm is not None else None
-    a.perm_q = a.perm_kv = a.o_row_map = p
+    a.residue_stride = s
     a.pred = _lib.PaPred(*spec)
     a.scale = 0.0
     return a
 
 
-@pytest.mark.parametrize("name,spec,N,s,BQ,A", [
-    ("dilated-4 rp4", (O.DILATED, 4, 0, 0), 4096, 4, 128, 32),
-    ("sinks4+win512", (O.SINKS, 512, 4, 0), 2048, 0, 16, 16),
-])
-def test_noalloc_matches_workspace_path(name, spec, N, s, BQ, A):
+# two calls in a row: a dense index with a large work list first, then a sparser one
+# with another N, tile shape and basis, whose work list is smaller and laid out
+# differently in the same array
+SEQUENCES = {
+    "causal then dilated-4 rp4": [((O.CAUSAL, 0, 0, 0), 4096, 0, 128, 16),
+                                  ((O.DILATED, 4, 0, 0), 2048, 4, 128, 32)],
+    "dilated-4 rp4 then sinks": [((O.DILATED, 4, 0, 0), 4096, 4, 128, 32),
+                                 ((O.SINKS, 512, 4, 0), 2048, 0, 16, 16)],
+}
+
+
+@pytest.mark.parametrize("seq", sorted(SEQUENCES))
+def test_noalloc_matches_workspace_path(seq):
     from polyhedral_b200 import _lib, blockindex, masks, permute
     lib = _lib.load()
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
     stream = _lib.stream_handle(dev)
-    perm = permute.residue_perm_device(N, s, dev) if s else None
-    dbi = blockindex.build_device(masks.from_spec(*spec), N, BQ, A, perm_q=perm, perm_kv=perm,
-                                  device=dev)
     outs = []
-    for call in range(2):
+    for call, (spec, N, s, BQ, A) in enumerate(SEQUENCES[seq]):
+        perm = permute.residue_perm_device(N, s, dev) if s else None
+        dbi = blockindex.build_device(masks.from_spec(*spec), N, BQ, A, perm_q=perm,
+                                      perm_kv=perm, device=dev)
         g = torch.Generator(device=dev).manual_seed(100 + call)
         q, k, v = (torch.randn(4, N, 128, device=dev, generator=g).bfloat16() for _ in range(3))
         o_ref, o_na = torch.empty_like(q), torch.full_like(q, float("nan"))
         l_ref = torch.empty(4, N, device=dev)
         l_na = torch.full((4, N), float("nan"), device=dev)
         # existing entry point with a caller-allocated workspace
-        a = _args(q, k, v, o_ref, l_ref, dbi, spec, perm, BQ, A)
+        a = _args(q, k, v, o_ref, l_ref, dbi, spec, s, BQ, A)
         nbytes = lib.pa_attn_workspace_size(ctypes.byref(a))
         ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         assert lib.pa_attn_plan(ctypes.byref(a), ws.data_ptr(), nbytes, stream) == 0
         assert lib.pa_attn_fwd(ctypes.byref(a), ws.data_ptr(), nbytes, stream) == 0
-        # the entry point that allocates nothing
-        b = _args(q, k, v, o_na, l_na, dbi, spec, perm, BQ, A)
+        st = ctypes.c_int32(-1)
+        assert lib.pa_attn_status(ws.data_ptr(), ctypes.byref(st), stream) == 0 and st.value == 0
+        # the entry point that allocates nothing, and its own status word
+        b = _args(q, k, v, o_na, l_na, dbi, spec, s, BQ, A)
         rc = lib.pa_attn_fwd_noalloc(ctypes.byref(b), stream)
         assert rc == 0, lib.pa_last_error()
-        torch.cuda.synchronize(dev)
-        st = ctypes.c_int32(0)
-        assert lib.pa_attn_status(ws.data_ptr(), ctypes.byref(st), stream) == 0
-        # same kernels on the same inputs: identical within the suite's tolerance
-        diff = (o_na.float() - o_ref.float()).abs()
-        assert (diff <= 2e-2 + 1e-2 * o_ref.float().abs()).all(), diff.max().item()
-        fin = torch.isfinite(l_ref)
-        assert torch.equal(torch.isfinite(l_na), fin)
-        assert (l_na[fin] - l_ref[fin]).abs().max().item() <= 2e-2
-        outs.append(o_na.clone())
-    assert not torch.equal(outs[0], outs[1])   # the two calls really had different inputs
+        st = ctypes.c_int32(-1)
+        rc = lib.pa_attn_noalloc_status(ctypes.byref(st), stream)
+        assert rc == 0 and st.value == 0, (rc, st.value, lib.pa_last_error())
+        # the same kernels on the same inputs: bit-identical results
+        assert torch.equal(o_na, o_ref)
+        assert torch.equal(l_na, l_ref)
+        outs.append(o_na.float().abs().sum().item())
+    assert outs[0] != outs[1]   # the two calls really computed different things
 
 
 def test_noalloc_rejects_oversize_request():
