@@ -153,6 +153,67 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// d = a * b + c on two lanes at once (f32x2), every operand a pair.
+__device__ __forceinline__ void fma2v(float& d0, float& d1, float a0, float a1, float b0,
+                                      float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// Pairs (index i = 0..15 of each 32-column chunk of a row) whose exponentials run on
+// the FMA pipe (exp2_fma) instead of the XU pipe.  On B200 ex2 is the softmax's only
+// XU instruction, at 8 cycles per warp instruction per scheduler: the exponentials of
+// a 128 x 128 tile take the XU as long as the tensor core takes for the tile's two
+// MMAs.  Measured on the forward kernels (c2, c3, c4, c5; 4, 5 and 8 of 16 pairs):
+// no faster with 4, slower with more -- the per-half chain, not the XU, sets the
+// kernel's period -- so no pair is moved by default.
+#ifndef PA_FMA_EXP_PAIRS
+#define PA_FMA_EXP_PAIRS 0u
+#endif
+constexpr uint32_t kFmaExpPairs = PA_FMA_EXP_PAIRS;
+
+// 2^x for two values on the FMA and integer pipes, no XU instruction: x = j + f with
+// j = rint(x), read from the low mantissa bits of t = x + 1.5 * 2^23 (the add rounds
+// to the nearest integer; 1.5 * 2^23 keeps t in [2^23, 2^24) for |x| < 2^22);
+// 2^f by a cubic on [-1/2, 1/2] fitted for least maximum relative error (7.5e-5, well
+// below the bf16 rounding P gets next); 2^j as the float whose exponent field is
+// j + 127, made by one integer multiply-add on t's bits ((j mod 2^9) << 23 plus the
+// bits of 1.0f, mod 2^32).  x is clamped to >= -127 first, where that field is 0: the
+// scale is exactly 0, so a masked score (-inf) gives exactly 0, as ex2.approx.ftz
+// does.  Used for x <= 127 (the softmax's x never exceeds the lazy-rescale margin).
+__device__ __forceinline__ void exp2_fma(float x0, float x1, float& y0, float& y1) {
+  constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+  constexpr float kC0 = 0.99992811f, kC1 = 0.69326097f, kC2 = 0.24261054f, kC3 = 0.055171322f;
+  x0 = fmaxf(x0, -127.0f);
+  x1 = fmaxf(x1, -127.0f);
+  float t0, t1, j0, j1, f0, f1, p0, p1;
+  fma2v(t0, t1, x0, x1, 1.0f, 1.0f, kRound, kRound);        // t = x + R
+  fma2v(j0, j1, t0, t1, 1.0f, 1.0f, -kRound, -kRound);      // j = t - R (exact)
+  fma2v(f0, f1, j0, j1, -1.0f, -1.0f, x0, x1);              // f = x - j
+  fma2v(p0, p1, f0, f1, kC3, kC3, kC2, kC2);
+  fma2v(p0, p1, p0, p1, f0, f1, kC1, kC1);
+  fma2v(p0, p1, p0, p1, f0, f1, kC0, kC0);
+  const float s0 = __uint_as_float(__float_as_uint(t0) * 8388608u + 0x3F800000u);
+  const float s1 = __uint_as_float(__float_as_uint(t1) * 8388608u + 0x3F800000u);
+  fma2v(y0, y1, p0, p1, s0, s1, 0.0f, 0.0f);               // 2^f * 2^j
+}
+
+// The exponentials of pair i of a 32-column chunk (i a compile-time constant after
+// unrolling): on the FMA pipe for the pairs in kFmaExpPairs, on the XU otherwise.
+__device__ __forceinline__ void exp2_pair(int i, float x0, float x1, float& y0, float& y1) {
+  if ((kFmaExpPairs >> i) & 1u) {
+    exp2_fma(x0, x1, y0, y1);
+  } else {
+    y0 = ex2(x0);
+    y1 = ex2(x1);
+  }
+}
+
 template <bool kBf16>
 __device__ __forceinline__ void unpack2(uint32_t u, float& lo, float& hi) {
   if constexpr (kBf16) {
@@ -218,113 +279,6 @@ __device__ __forceinline__ SegInfo seg_info(const FwdParams& P, const int32_t* e
   const int sub = P.A / BN;
   const int e = u / sub;
   return SegInfo{__ldg(ent + e) * P.A + (u - e * sub) * BN, (int)__ldg(sts + e)};
-}
-
-// floor(a / b) for b > 0
-__device__ __forceinline__ int floordiv(int a, int b) {
-  return a >= 0 ? a / b : -((-a + b - 1) / b);
-}
-
-// Bits (c - base) for c in [lo, hi], clipped to the word [base, base + 32).
-__device__ __forceinline__ uint32_t range_bits(int lo, int hi, int base) {
-  lo = max(lo - base, 0);
-  hi = min(hi - base, 31);
-  if (hi < lo) return 0u;
-  const uint32_t upto = hi == 31 ? 0xffffffffu : ((2u << hi) - 1u);
-  return upto & ~((1u << lo) - 1u);
-}
-
-// Live bits of columns [base, base + 32) of a segment of `len` columns whose
-// original indices form the progression j0 + c*dj (dj >= 1), for the row with
-// original index i = j0 + e.  With d = e - c*dj decreasing in c, every kind is a
-// union of at most two ranges of c, and a lattice term (d % m == 0) is constant
-// over the segment when m divides dj, and every m-th column when dj = 1 and m is a
-// power of two.  Returns false otherwise (the caller then evaluates element by
-// element).
-__device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, int dj, int sh,
-                                                 int base, int len, uint32_t& out) {
-  // floor(a / dj): an arithmetic shift when dj is a power of two (sh >= 0)
-  auto fdiv = [&](int a) { return sh >= 0 ? (a >> sh) : floordiv(a, dj); };
-  const int cz = fdiv(e);                               // d >= 0  <=>  c <= cz
-  int lo1 = 0, hi1 = -1, lo2 = 0, hi2 = -1;
-  bool lattice = false;
-  if (p.mod > 0) {
-    if (!divisible(dj, p.mod, p.inv_mod)) {
-      // Unit column step (no permutation) and a power-of-two modulus: the lattice
-      // columns are every mod-th one, a shifted periodic pattern.
-      if (dj != 1 || p.mod > 32 || (p.mod & (p.mod - 1))) return false;
-      const uint32_t pat = p.mod == 2 ? 0x55555555u : p.mod == 4 ? 0x11111111u
-                           : p.mod == 8 ? 0x01010101u : p.mod == 16 ? 0x00010001u : 1u;
-      const uint32_t lat = e >= 0 ? pat << ((e - base) & (p.mod - 1)) : 0u;
-      int hi = cz;
-      uint32_t near = 0u;
-      switch (p.kind) {
-        case PA_DILATED:
-          break;
-        case PA_FAR_STRIDED:
-          hi = min(cz, fdiv(e - p.p0));
-          break;
-        case PA_LOCAL_STRIDED:
-          near = range_bits(fdiv(e - p.p0) + 1, min(cz, len - 1), base);
-          break;
-        default:
-          return false;
-      }
-      out = (range_bits(0, min(hi, len - 1), base) & lat) | near;
-      return true;
-    }
-    lattice = e >= 0 && divisible(e, p.mod, p.inv_mod);   // only e >= 0 can reach c <= cz
-  }
-  switch (p.kind) {
-    case PA_CAUSAL:
-      hi1 = cz;
-      break;
-    case PA_WINDOW:                                     // d < p0 <=> c > (e - p0) / dj
-      lo1 = fdiv(e - p.p0) + 1;
-      hi1 = cz;
-      break;
-    case PA_DILATED:
-      hi1 = lattice ? cz : -1;
-      break;
-    case PA_LOCAL_STRIDED:
-      lo1 = fdiv(e - p.p0) + 1;
-      hi1 = cz;
-      hi2 = lattice ? cz : -1;
-      break;
-    case PA_TWOBAND:
-      lo1 = fdiv(e - p.p0) + 1;
-      hi1 = cz;
-      lo2 = fdiv(e - p.p1 - p.p2) + 1;
-      hi2 = min(cz, fdiv(e - p.p1));
-      break;
-    case PA_SINKS:                                      // kv < p1 <=> c <= (p1 - j0 - 1) / dj
-      lo1 = fdiv(e - p.p0) + 1;
-      hi1 = cz;
-      hi2 = min(cz, fdiv(p.p1 - j0 - 1));
-      break;
-    case PA_FAR_STRIDED:                                // d >= p0 <=> c <= (e - p0) / dj
-      hi1 = lattice ? min(cz, fdiv(e - p.p0)) : -1;
-      break;
-    default:
-      return false;
-  }
-  hi1 = min(hi1, len - 1);
-  hi2 = min(hi2, len - 1);
-  out = range_bits(lo1, hi1, base) | range_bits(lo2, hi2, base);
-  return true;
-}
-
-// Live bits of `n` (<= 32) columns evaluated one by one; column c has original
-// index cols[c] (global memory) when given, else j0 + (base + c) * dj.
-__device__ __forceinline__ uint32_t element_bits(const Pred& p, int i, const int* cols, int j0,
-                                                 int dj, int base, int n) {
-  uint32_t w = 0;
-#pragma unroll 1
-  for (int c = 0; c < n; ++c) {
-    const int j = cols ? __ldg(cols + c) : j0 + (base + c) * dj;
-    w |= (uint32_t)pred_live(p, i, j) << c;
-  }
-  return w;
 }
 
 // d = a * b + c on two lanes at once (f32x2).
@@ -920,8 +874,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
               const int c = q4 * 32 + 2 * i;
               float x0, x1;
               ffma2(x0, x1, s[c], s[c + 1], c2, -msub);
-              const float a = ex2(x0);
-              const float b = ex2(x1);
+              float a, b;
+              exp2_pair(i, x0, x1, a, b);
               const int j = (2 * i) & 7;
               fadd2(r8[j], r8[j + 1], a, b);
               pk[i] = pack2<kBf16>(a, b);
@@ -1220,8 +1174,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
             const int c = q4 * 32 + 2 * i;
             float x0, x1;
             ffma2(x0, x1, s[c], s[c + 1], c2, -msub);
-            const float a = ex2(x0);
-            const float b = ex2(x1);
+            float a, b;
+            exp2_pair(i, x0, x1, a, b);
             const int j = (2 * i) & 7;
             fadd2(r8[j], r8[j + 1], a, b);
             pk[i] = pack2<kBf16>(a, b);

@@ -488,8 +488,8 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
             const int c = q2 * 32 + 2 * i;
             float x0, x1;
             ffma2(x0, x1, s[c], s[c + 1], c2, -msub);
-            const float a = ex2(x0);
-            const float b2 = ex2(x1);
+            float a, b2;
+            exp2_pair(i, x0, x1, a, b2);
             const int j = (2 * i) & 7;
             fadd2(r8[j], r8[j + 1], a, b2);
             pk[i] = pack2<kBf16>(a, b2);

@@ -2,13 +2,13 @@
 // dead / full / partial and writes the reference's BlockIndex arrays
 // (gpu/blockindex.py:32-51) without materialising the N x N mask.
 //
-// One CTA per query block.  Each warp takes column tiles in turn; a column
-// permutation is staged in shared memory first when it fits.  A tile is
-// first decided from bounds alone -- the min/max original coordinate of its rows
-// and columns and, for lattice kinds, whether all rows (columns) share one
-// residue modulo the lattice stride, which makes the lattice term constant over
-// the tile (the usual case under a residue permutation).  Tiles the bounds cannot
-// decide are enumerated element by element.  Live tiles are then compacted in
+// One CTA per query block; a column permutation is staged in shared memory first
+// when it fits.  Every tile is first decided from bounds alone, one tile per
+// thread -- the min/max original coordinate of its rows and columns and, for
+// lattice kinds, whether all rows (columns) share one residue modulo the lattice
+// stride, which makes the lattice term constant over the tile (the usual case under
+// a residue permutation).  Tiles the bounds cannot decide are queued and enumerated
+// element by element, one warp per tile.  Live tiles are then compacted in
 // ascending column order with a block-wide scan, so kv_idx is bit-identical to
 // the reference's np.flatnonzero order.
 #include <climits>
@@ -23,7 +23,8 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxTilesPerRow = 65536;   // N / A, bounded by the flag array in shared memory
 constexpr int kMaxBQ = 4096;
 
-enum : uint8_t { T_DEAD = 0, T_FULL = 1, T_PARTIAL = 2 };
+enum : uint8_t { T_DEAD = 0, T_FULL = 1, T_PARTIAL = 2, T_QUEUED = 3, T_OVERFLOW = 4 };
+constexpr int kUndCap = 1024;            // undecided tiles queued per row block
 
 // 0 = dead, 1 = full, 3 = undecided.  Exact whenever it decides.
 __device__ int classify_bounds(const Pred& p, int imin, int imax, int jmin, int jmax,
@@ -69,6 +70,19 @@ __device__ int classify_bounds(const Pred& p, int imin, int imax, int jmin, int 
       return 3;
   }
   return 3;
+}
+
+// Live bits of `n` (<= 32) columns evaluated one by one; column c has original index
+// cols[c] when given -- shared memory (the staged permutation) or global memory, so a
+// generic load, not element_bits' read-only global load -- else j0 + (base + c) * dj.
+__device__ uint32_t element_bits_any(const Pred& p, int i, const int* cols, int j0, int dj,
+                                     int base, int n) {
+  uint32_t w = 0;
+  for (int c = 0; c < n; ++c) {
+    const int j = cols ? cols[c] : j0 + (base + c) * dj;
+    w |= (uint32_t)pred_live(p, i, j) << c;
+  }
+  return w;
 }
 
 __device__ __forceinline__ int warp_min(int v) {
@@ -121,6 +135,8 @@ block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ 
   __shared__ int s_warp[kWarps];
   __shared__ int s_red[4];
   __shared__ unsigned long long s_live;
+  __shared__ int s_nund;                 // tiles the bounds left undecided
+  __shared__ int s_und[kUndCap];
 
   const int nk = N / A;
   const int rb = blockIdx.x;
@@ -128,7 +144,7 @@ block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ 
   const int mod = pred.mod;
 
   if (threadIdx.x == 0) {
-    s_red[0] = INT_MAX; s_red[1] = INT_MIN; s_red[2] = 1; s_live = 0ull;
+    s_red[0] = INT_MAX; s_red[1] = INT_MIN; s_red[2] = 1; s_live = 0ull; s_nund = 0;
   }
   for (int r = threadIdx.x; r < BQ; r += kThreads) {
     const int row = rb * BQ + r;
@@ -161,34 +177,92 @@ block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ 
   const bool iuni = s_red[2] != 0;
   const int ires = mod > 1 ? rows_i[0] % mod : 0;
 
-  unsigned long long live_w = 0;
-  for (int t = warp; t < nk; t += kWarps) {
+  // Pass 1, one tile per thread: every tile the bounds decide.  Column bounds are
+  // closed-form for identity columns and read from the (staged) permutation otherwise.
+  // Tiles the bounds cannot decide go to a queue the warps then share, so that the
+  // few partial tiles of a row block are enumerated by different warps.
+  unsigned long long live_t = 0;
+  for (int t = threadIdx.x; t < nk; t += kThreads) {
     const int c0 = t * A;
     int cls = 3;
     if (!dense) {
-      int mn = INT_MAX, mx = INT_MIN, uni = 1;
-      const int j0 = cols ? cols[c0] : c0;
-      const int jres = mod > 1 ? j0 % mod : 0;
-      for (int c = lane; c < A; c += 32) {
-        const int j = cols ? cols[c0 + c] : c0 + c;
-        mn = min(mn, j); mx = max(mx, j);
-        if (mod > 1 && j % mod != jres) uni = 0;
+      int mn, mx, uni = 1, jres;
+      if (!cols) {
+        mn = c0;
+        mx = c0 + A - 1;
+        jres = mod > 1 ? c0 % mod : 0;
+        uni = A == 1;                       // consecutive columns: mixed residues
+      } else {
+        mn = mx = cols[c0];
+        jres = mod > 1 ? mn % mod : 0;
+        for (int c = 1; c < A; ++c) {
+          const int j = cols[c0 + c];
+          mn = min(mn, j);
+          mx = max(mx, j);
+          if (mod > 1 && j % mod != jres) uni = 0;
+        }
       }
-      mn = warp_min(mn); mx = warp_max(mx);
-      uni = __all_sync(0xffffffffu, uni);
       const bool uniform = (mod <= 1) || (iuni && uni);
       const int dres = mod > 1 ? (((ires - jres) % mod) + mod) % mod : 0;
       cls = classify_bounds(pred, imin, imax, mn, mx, uniform, dres);
     }
-    uint8_t flag;
-    if (cls == 0) {
-      flag = T_DEAD;
-    } else if (cls == 1) {
+    uint8_t flag = T_DEAD;
+    if (cls == 1) {
       flag = T_FULL;
-      live_w += (unsigned long long)BQ * A;
+      live_t += (unsigned long long)BQ * A;
+    } else if (cls == 3) {
+      const int k = atomicAdd(&s_nund, 1);
+      if (k < kUndCap) {
+        s_und[k] = t;
+        flag = T_QUEUED;
+      } else {
+        flag = T_OVERFLOW;                  // enumerated by the strided pass below
+      }
+    }
+    flags[t] = flag;
+  }
+  if (live_t) atomicAdd(&s_live, live_t);
+  __syncthreads();
+
+  // Pass 2, one warp per undecided tile, counting live elements.  Mask kinds whose
+  // live columns of a row form at most two ranges of a column progression (every
+  // kind here, when the tile's columns are j0 + c*dj) are counted a row per lane, 32
+  // columns per word in closed form (progression_bits); other tiles element by element.
+  unsigned long long live_w = 0;
+  auto enumerate = [&](int t) {
+    const int c0 = t * A;
+    int any = 0, all = 1;
+    unsigned long long cnt = 0;
+    bool ap = false;
+    int j0 = c0, dj = 1;
+    if (!dense) {
+      ap = true;
+      if (cols) {
+        j0 = cols[c0];
+        dj = A > 1 ? cols[c0 + 1] - j0 : 1;
+        int ok = dj >= 1;
+        for (int c = lane; c < A && ok; c += 32) ok = cols[c0 + c] == j0 + c * dj;
+        ap = __all_sync(0xffffffffu, ok);
+      }
+    }
+    if (ap) {
+      const int sh = (dj & (dj - 1)) == 0 ? 31 - __clz(dj) : -1;
+      for (int r = lane; r < BQ; r += 32) {
+        const int i = rows_i[r];
+        for (int base = 0; base < A; base += 32) {
+          const int width = min(32, A - base);
+          const uint32_t full = width == 32 ? 0xffffffffu : ((1u << width) - 1u);
+          uint32_t w;
+          if (!progression_bits(pred, i - j0, j0, dj, sh, base, A, w))
+            w = element_bits_any(pred, i, cols ? cols + c0 + base : nullptr, j0, dj, base, width);
+          w &= full;
+          cnt += __popc(w);
+          any |= w != 0u;
+          all &= w == full;
+        }
+      }
     } else {
-      // enumerate the tile: element e = r * A + c, lanes stride by 32
-      int any = 0, all = 1, cnt = 0;
+      // element by element (e = r * A + c, lanes stride by 32)
       int r = lane / A, c = lane % A;
       const int total = BQ * A;
       for (int e = lane; e < total; e += 32) {
@@ -203,14 +277,18 @@ block_index_kernel(Pred pred, int N, int BQ, int A, const int32_t* __restrict__ 
         c += 32;
         while (c >= A) { c -= A; ++r; }
       }
-      any = __any_sync(0xffffffffu, any);
-      all = __all_sync(0xffffffffu, all);
-      cnt = __reduce_add_sync(0xffffffffu, cnt);
-      flag = any ? (all ? T_FULL : T_PARTIAL) : T_DEAD;
-      live_w += (unsigned long long)cnt;
     }
-    if (lane == 0) flags[t] = flag;
-  }
+    any = __any_sync(0xffffffffu, any);
+    all = __all_sync(0xffffffffu, all);
+    for (int o = 16; o; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    if (lane == 0) flags[t] = any ? (all ? T_FULL : T_PARTIAL) : T_DEAD;
+    live_w += cnt;
+  };
+  const int nund = min(s_nund, kUndCap);
+  for (int k = warp; k < nund; k += kWarps) enumerate(s_und[k]);
+  if (s_nund > kUndCap)
+    for (int t = warp; t < nk; t += kWarps)
+      if (flags[t] == T_OVERFLOW) enumerate(t);
   if (lane == 0 && live_w) atomicAdd(&s_live, live_w);
   __syncthreads();
 

@@ -286,4 +286,112 @@ PA_DEV bool pred_live(const Pred& p, int i, int j) {
   }
 }
 
+// ------------------------------------------------------------------ live bits
+// floor(a / b) for b > 0
+__device__ __forceinline__ int floordiv(int a, int b) {
+  return a >= 0 ? a / b : -((-a + b - 1) / b);
+}
+
+// Bits (c - base) for c in [lo, hi], clipped to the word [base, base + 32).
+__device__ __forceinline__ uint32_t range_bits(int lo, int hi, int base) {
+  lo = max(lo - base, 0);
+  hi = min(hi - base, 31);
+  if (hi < lo) return 0u;
+  const uint32_t upto = hi == 31 ? 0xffffffffu : ((2u << hi) - 1u);
+  return upto & ~((1u << lo) - 1u);
+}
+
+// Live bits of columns [base, base + 32) of a segment of `len` columns whose
+// original indices form the progression j0 + c*dj (dj >= 1), for the row with
+// original index i = j0 + e.  With d = e - c*dj decreasing in c, every kind is a
+// union of at most two ranges of c, and a lattice term (d % m == 0) is constant
+// over the segment when m divides dj, and every m-th column when dj = 1 and m is a
+// power of two.  Returns false otherwise (the caller then evaluates element by
+// element).
+__device__ __forceinline__ bool progression_bits(const Pred& p, int e, int j0, int dj, int sh,
+                                                 int base, int len, uint32_t& out) {
+  // floor(a / dj): an arithmetic shift when dj is a power of two (sh >= 0)
+  auto fdiv = [&](int a) { return sh >= 0 ? (a >> sh) : floordiv(a, dj); };
+  const int cz = fdiv(e);                               // d >= 0  <=>  c <= cz
+  int lo1 = 0, hi1 = -1, lo2 = 0, hi2 = -1;
+  bool lattice = false;
+  if (p.mod > 0) {
+    if (!divisible(dj, p.mod, p.inv_mod)) {
+      // Unit column step (no permutation) and a power-of-two modulus: the lattice
+      // columns are every mod-th one, a shifted periodic pattern.
+      if (dj != 1 || p.mod > 32 || (p.mod & (p.mod - 1))) return false;
+      const uint32_t pat = p.mod == 2 ? 0x55555555u : p.mod == 4 ? 0x11111111u
+                           : p.mod == 8 ? 0x01010101u : p.mod == 16 ? 0x00010001u : 1u;
+      const uint32_t lat = e >= 0 ? pat << ((e - base) & (p.mod - 1)) : 0u;
+      int hi = cz;
+      uint32_t near = 0u;
+      switch (p.kind) {
+        case PA_DILATED:
+          break;
+        case PA_FAR_STRIDED:
+          hi = min(cz, fdiv(e - p.p0));
+          break;
+        case PA_LOCAL_STRIDED:
+          near = range_bits(fdiv(e - p.p0) + 1, min(cz, len - 1), base);
+          break;
+        default:
+          return false;
+      }
+      out = (range_bits(0, min(hi, len - 1), base) & lat) | near;
+      return true;
+    }
+    lattice = e >= 0 && divisible(e, p.mod, p.inv_mod);   // only e >= 0 can reach c <= cz
+  }
+  switch (p.kind) {
+    case PA_CAUSAL:
+      hi1 = cz;
+      break;
+    case PA_WINDOW:                                     // d < p0 <=> c > (e - p0) / dj
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      break;
+    case PA_DILATED:
+      hi1 = lattice ? cz : -1;
+      break;
+    case PA_LOCAL_STRIDED:
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      hi2 = lattice ? cz : -1;
+      break;
+    case PA_TWOBAND:
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      lo2 = fdiv(e - p.p1 - p.p2) + 1;
+      hi2 = min(cz, fdiv(e - p.p1));
+      break;
+    case PA_SINKS:                                      // kv < p1 <=> c <= (p1 - j0 - 1) / dj
+      lo1 = fdiv(e - p.p0) + 1;
+      hi1 = cz;
+      hi2 = min(cz, fdiv(p.p1 - j0 - 1));
+      break;
+    case PA_FAR_STRIDED:                                // d >= p0 <=> c <= (e - p0) / dj
+      hi1 = lattice ? min(cz, fdiv(e - p.p0)) : -1;
+      break;
+    default:
+      return false;
+  }
+  hi1 = min(hi1, len - 1);
+  hi2 = min(hi2, len - 1);
+  out = range_bits(lo1, hi1, base) | range_bits(lo2, hi2, base);
+  return true;
+}
+
+// Live bits of `n` (<= 32) columns evaluated one by one; column c has original
+// index cols[c] (global memory) when given, else j0 + (base + c) * dj.
+__device__ __forceinline__ uint32_t element_bits(const Pred& p, int i, const int* cols, int j0,
+                                                 int dj, int base, int n) {
+  uint32_t w = 0;
+#pragma unroll 1
+  for (int c = 0; c < n; ++c) {
+    const int j = cols ? __ldg(cols + c) : j0 + (base + c) * dj;
+    w |= (uint32_t)pred_live(p, i, j) << c;
+  }
+  return w;
+}
+
 }  // namespace pa

@@ -4,8 +4,8 @@
 //
 // HBM-bound: each output row reads two O rows and two LSE values and writes one
 // O row and one LSE.  A row is handled by D/8 threads, each moving 16 bytes
-// (8 elements) per input, so a 256-thread CTA covers 16 rows at D = 128 per step of
-// its grid-stride loop (8 CTAs per SM).
+// (8 elements) per input; a 256-thread CTA takes 64 rows of one head per step of its
+// grid-stride loop at D = 128, four per thread, all loads issued before any use.
 #include <math.h>
 #include "common.cuh"
 #include "capi_util.h"
@@ -54,90 +54,90 @@ struct Vec8<__half> {
   }
 };
 
-// One output row as one thread sees it: its 8-column share of O1 and O2 and the
-// row's two LSE values (D / 8 <= 32 threads cover a row, one chunk each).
-template <typename T>
-struct RowIn {
-  long long g;      // flattened (bh, row), or >= BH * N when past the end
-  int bh, row;
-  bool valid, r2_ok;
-  float l1, l2;
-  uint4 x1, x2;
-};
-
-template <typename T>
-__device__ __forceinline__ void load_row(const pa_merge_args& a, long long g, long long total,
-                                         int c, RowIn<T>& r) {
-  r.g = g;
-  r.valid = g < total && c < a.D;
-  const bool in = g < total;
-  r.bh = in ? (int)(g / a.N) : 0;
-  r.row = in ? (int)(g - (long long)r.bh * a.N) : 0;
-  const int r2 = !in ? -1 : (a.row_map2 ? a.row_map2[r.row] : r.row);
-  r.r2_ok = (unsigned)r2 < (unsigned)a.N;
-  r.l1 = in ? a.lse1[(long long)r.bh * a.lse1_bh_stride + r.row] : -INFINITY;
-  r.l2 = r.r2_ok ? a.lse2[(long long)r.bh * a.lse2_bh_stride + r2] : -INFINITY;
-  r.x1 = r.x2 = make_uint4(0u, 0u, 0u, 0u);
-  if (r.valid) {
-    const T* o1 = static_cast<const T*>(a.o1) + (long long)r.bh * a.o1_bh_stride +
-                  (long long)r.row * a.o1_row_stride;
-    r.x1 = *reinterpret_cast<const uint4*>(o1 + c);
-    if (r.r2_ok) {
-      const T* o2 = static_cast<const T*>(a.o2) + (long long)r.bh * a.o2_bh_stride +
-                    (long long)r2 * a.o2_row_stride;
-      r.x2 = *reinterpret_cast<const uint4*>(o2 + c);
-    }
-  }
-}
-
 // m = max(l1, l2); O = (e^(l1-m) O1 + e^(l2-m) O2) / (e^(l1-m) + e^(l2-m));
-// LSE = m + log(e^(l1-m) + e^(l2-m)); both -inf -> O = 0, LSE = -inf.
-template <typename T>
-__device__ __forceinline__ float store_row(const pa_merge_args& a, int c, const RowIn<T>& r) {
-  const float m = fmaxf(r.l1, r.l2);
-  float w1 = 0.f, w2 = 0.f;
+// LSE = m + log(e^(l1-m) + e^(l2-m)); both -inf -> O = 0, LSE = -inf.  Returns the
+// two weights folded into w1 / w2 and the merged LSE.
+__device__ __forceinline__ float merge_weights(float l1, float l2, float& w1, float& w2) {
+  const float m = fmaxf(l1, l2);
+  w1 = 0.f;
+  w2 = 0.f;
   if (m != -INFINITY) {
-    w1 = expf(r.l1 - m);
-    w2 = expf(r.l2 - m);
+    w1 = expf(l1 - m);
+    w2 = expf(l2 - m);
   }
   const float den = w1 + w2;
   const float inv = den > 0.f ? 1.f / den : 0.f;
   w1 *= inv;
   w2 *= inv;
-  if (r.valid) {
-    float x1[8], x2[8], y[8];
-    Vec8<T>::to_float(r.x1, x1);
-    Vec8<T>::to_float(r.x2, x2);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = w1 * x1[i] + w2 * x2[i];
-    T* o = static_cast<T*>(a.o) + (long long)r.bh * a.o_bh_stride + (long long)r.row * a.o_row_stride;
-    *reinterpret_cast<uint4*>(o + c) = Vec8<T>::from_float(y);
-  }
   return den > 0.f ? m + logf(den) : -INFINITY;
 }
 
+constexpr int kThreads = 256;
+constexpr int kRows = 4;   // rows per thread per chunk: all their loads are issued first
+
+// Grid-stride over chunks of kRows * (256 / tpr) consecutive rows of one (b, h): the
+// chunk's head and first row come from one 64-bit division per chunk.  Thread
+// (slot, part) handles columns [8 part, 8 part + 8) of rows slot, slot + rpp, ...;
+// every load of its kRows rows is in flight before the first use (kRows x 32 bytes
+// of O plus the LSE values per thread), which is what keeps HBM busy.
 template <typename T>
-__global__ void __launch_bounds__(256) lse_merge_kernel(pa_merge_args a, int tpr) {
-  // Grid-stride over the flattened (bh, row) rows, two rows per thread per step
-  // with all of both rows' loads issued before any arithmetic, so that each thread
-  // keeps four 16-byte loads in flight.  Every thread runs the same number of steps
-  // (the warp-level sync stays uniform); rows past the end are masked.
-  const int rows_per_cta = 256 / tpr;
+__global__ void __launch_bounds__(kThreads, 3) lse_merge_kernel(pa_merge_args a, int tpr) {
+  const int rpp = kThreads / tpr;               // rows per pass of the CTA
   const int part = threadIdx.x % tpr;
+  const int slot = threadIdx.x / tpr;
   const int c = part * 8;
-  const long long total = (long long)a.BH * a.N;
-  const long long step = (long long)gridDim.x * rows_per_cta * 2;
-  for (long long base = (long long)blockIdx.x * rows_per_cta * 2; base < total; base += step) {
-    const long long g0 = base + threadIdx.x / tpr;
-    RowIn<T> r0, r1;
-    load_row<T>(a, g0, total, c, r0);
-    load_row<T>(a, g0 + rows_per_cta, total, c, r1);
-    const float lse0 = store_row<T>(a, c, r0);
-    const float lse1 = store_row<T>(a, c, r1);
+  const bool col_ok = c < a.D;
+  const int chunk_rows = kRows * rpp;
+  const long long cpb = (a.N + chunk_rows - 1) / chunk_rows;   // chunks per (b, h)
+  const long long nchunks = cpb * a.BH;
+  for (long long ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+    const int bh = (int)(ch / cpb);
+    const int row0 = (int)(ch - (long long)bh * cpb) * chunk_rows;
+    uint4 x1[kRows], x2[kRows];
+    float l1[kRows], l2[kRows];
+    int rows[kRows];
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      const int row = row0 + slot + k * rpp;
+      rows[k] = row;
+      const bool in = row < a.N;
+      const int r2 = !in ? -1 : (a.row_map2 ? a.row_map2[row] : row);
+      const bool r2_ok = (unsigned)r2 < (unsigned)a.N;
+      l1[k] = in ? a.lse1[(long long)bh * a.lse1_bh_stride + row] : -INFINITY;
+      l2[k] = r2_ok ? a.lse2[(long long)bh * a.lse2_bh_stride + r2] : -INFINITY;
+      x1[k] = x2[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (in && col_ok) {
+        const T* o1 = static_cast<const T*>(a.o1) + (long long)bh * a.o1_bh_stride +
+                      (long long)row * a.o1_row_stride + c;
+        x1[k] = *reinterpret_cast<const uint4*>(o1);
+        if (r2_ok) {
+          const T* o2 = static_cast<const T*>(a.o2) + (long long)bh * a.o2_bh_stride +
+                        (long long)r2 * a.o2_row_stride + c;
+          x2[k] = *reinterpret_cast<const uint4*>(o2);
+        }
+      }
+    }
+    float lse[kRows];
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      float w1, w2;
+      lse[k] = merge_weights(l1[k], l2[k], w1, w2);
+      if (rows[k] < a.N && col_ok) {
+        float f1[8], f2[8], y[8];
+        Vec8<T>::to_float(x1[k], f1);
+        Vec8<T>::to_float(x2[k], f2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = w1 * f1[i] + w2 * f2[i];
+        T* o = static_cast<T*>(a.o) + (long long)bh * a.o_bh_stride +
+               (long long)rows[k] * a.o_row_stride + c;
+        *reinterpret_cast<uint4*>(o) = Vec8<T>::from_float(y);
+      }
+    }
     __syncwarp();   // every lane of these rows has read lse1 before it may be overwritten
     if (part == 0) {
-      if (r0.g < total) a.lse[(long long)r0.bh * a.lse_bh_stride + r0.row] = lse0;
-      if (r1.g < total) a.lse[(long long)r1.bh * a.lse_bh_stride + r1.row] = lse1;
+#pragma unroll
+      for (int k = 0; k < kRows; ++k)
+        if (rows[k] < a.N) a.lse[(long long)bh * a.lse_bh_stride + rows[k]] = lse[k];
     }
   }
 }
@@ -164,16 +164,21 @@ extern "C" int pa_lse_merge(const pa_merge_args* a, pa_stream_t stream) {
                "pa_lse_merge: O pointers must be 16-byte aligned");
   int tpr = a->D / 8;
   if (tpr > 32) tpr = 32;
-  while (256 % tpr) --tpr;
-  const int rows_per_cta = 256 / tpr;
-  int dev = 0, sms = 148;
+  while (kThreads % tpr) --tpr;
+  const long long chunk_rows = (long long)kRows * (kThreads / tpr);
+  const long long nchunks = (a->N + chunk_rows - 1) / chunk_rows * a->BH;
+  int dev = 0, sms = 148, per_sm = 4;
   PA_CUDA(cudaGetDevice(&dev), "pa_lse_merge");
   PA_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "pa_lse_merge");
-  const long long steps = ((long long)a->BH * a->N + 2 * rows_per_cta - 1) / (2 * rows_per_cta);
-  const int grid = (int)(steps < 8LL * sms ? steps : 8LL * sms);
+  PA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+              &per_sm, a->dtype == PA_BF16 ? lse_merge_kernel<__nv_bfloat16> : lse_merge_kernel<__half>,
+              kThreads, 0), "pa_lse_merge");
+  // as many CTAs as are resident at once (grid-stride beyond that), no tail wave
+  const long long resident = (long long)sms * (per_sm > 0 ? per_sm : 1);
+  const int grid = (int)(nchunks < resident ? nchunks : resident);
   if (a->dtype == PA_BF16)
-    lse_merge_kernel<__nv_bfloat16><<<grid, 256, 0, (cudaStream_t)stream>>>(*a, tpr);
+    lse_merge_kernel<__nv_bfloat16><<<grid, kThreads, 0, (cudaStream_t)stream>>>(*a, tpr);
   else
-    lse_merge_kernel<__half><<<grid, 256, 0, (cudaStream_t)stream>>>(*a, tpr);
+    lse_merge_kernel<__half><<<grid, kThreads, 0, (cudaStream_t)stream>>>(*a, tpr);
   return check_launch("pa_lse_merge");
 }
