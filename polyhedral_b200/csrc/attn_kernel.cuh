@@ -5,6 +5,7 @@
 #pragma once
 #include <cuda.h>
 #include <math.h>
+#include <atomic>
 #include "common.cuh"
 #include "capi_util.h"
 
@@ -1408,6 +1409,19 @@ int launch_family(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdParam
     const int smem = kGather ? Smem<D, kCG>::kAllocGather : Smem<D, kCG>::kAlloc;
     PA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
             "pa_attn_fwd");
+    // the warpgroups' setmaxnreg shares must fit in the registers the CTA is launched
+    // with; a split above them would never complete, so refuse to launch instead
+    using R = Roles<kCG>;
+    static std::atomic<int> regs_ok{0};   // checked once per instantiation
+    cudaFuncAttributes fa;
+    fa.numRegs = 1 << 20;
+    if (!regs_ok.load(std::memory_order_relaxed))
+      PA_CUDA(cudaFuncGetAttributes(&fa, kernel), "pa_attn_fwd");
+    if (fa.numRegs * R::kThreads <
+        R::kSoftmaxWarps * 32 * R::kSoftmaxRegs + (R::kThreads - R::kSoftmaxWarps * 32) * R::kOtherRegs)
+      return fail(PA_ERR_UNSUPPORTED, "pa_attn_fwd: kernel built with %d registers per thread, "
+                  "below its register split", fa.numRegs);
+    regs_ok.store(1, std::memory_order_relaxed);
     kernel<<<grid, Roles<kCG>::kThreads, smem, stream>>>(tq, tk, tv, P);
     return PA_OK;
   };

@@ -611,6 +611,16 @@ int launch_family_db(const Tmap& tq, const Tmap& tk, const Tmap& tv, const FwdPa
     const int smem = Smem<D>::kAlloc;
     PA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
             "pa_attn_fwd");
+    // the warpgroups' setmaxnreg shares must fit in what the CTA is launched with
+    static std::atomic<int> regs_ok{0};   // checked once per instantiation
+    cudaFuncAttributes fa;
+    fa.numRegs = 1 << 20;
+    if (!regs_ok.load(std::memory_order_relaxed))
+      PA_CUDA(cudaFuncGetAttributes(&fa, kernel), "pa_attn_fwd");
+    if (fa.numRegs * kThreads < 2 * 128 * kSoftmaxRegs + 128 * kOtherRegs)
+      return fail(PA_ERR_UNSUPPORTED, "pa_attn_fwd: 64-row kernel built with %d registers per "
+                  "thread, below its register split", fa.numRegs);
+    regs_ok.store(1, std::memory_order_relaxed);
     kernel<<<grid, kThreads, smem, stream>>>(tq, tk, tv, P);
     return PA_OK;
   };
