@@ -3,9 +3,9 @@
 // argues for (and costs at :107-118) but never executes.
 //
 // HBM-bound: each output row reads two O rows and two LSE values and writes one
-// O row and one LSE.  A row is handled by D/8 threads, each moving 16 bytes
-// (8 elements) per input; a 256-thread CTA takes 64 rows of one head per step of its
-// grid-stride loop at D = 128, four per thread, all loads issued before any use.
+// O row and one LSE.  A row is handled by D/16 threads, each moving 32 bytes
+// (16 elements) per input; a 256-thread CTA takes 64 rows of one head per step of its
+// grid-stride loop at D = 128, two per thread, all loads issued before any use.
 #include <math.h>
 #include "common.cuh"
 #include "capi_util.h"
@@ -73,19 +73,21 @@ __device__ __forceinline__ float merge_weights(float l1, float l2, float& w1, fl
 }
 
 constexpr int kThreads = 256;
-constexpr int kRows = 4;   // rows per thread per chunk: all their loads are issued first
+constexpr int kRows = 2;   // rows per thread per chunk: all their loads are issued first
+constexpr int kVecs = 2;   // 16-byte vectors per thread per row (16 columns)
 
 // Grid-stride over chunks of kRows * (256 / tpr) consecutive rows of one (b, h): the
-// chunk's head and first row come from one 64-bit division per chunk.  Thread
-// (slot, part) handles columns [8 part, 8 part + 8) of rows slot, slot + rpp, ...;
-// every load of its kRows rows is in flight before the first use (kRows x 32 bytes
-// of O plus the LSE values per thread), which is what keeps HBM busy.
+// chunk's head and first row come from one 64-bit division per chunk, its base
+// pointers from one multiply.  Thread (slot, part) handles columns
+// [16 part, 16 part + 16) of rows slot, slot + rpp, ...: every load of its kRows rows
+// is in flight before the first use (kRows x 64 bytes of O plus the LSE values), and
+// the per-row work (addresses, weights) is shared by 32 bytes of each input.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 3) lse_merge_kernel(pa_merge_args a, int tpr) {
   const int rpp = kThreads / tpr;               // rows per pass of the CTA
   const int part = threadIdx.x % tpr;
   const int slot = threadIdx.x / tpr;
-  const int c = part * 8;
+  const int c = part * 8 * kVecs;
   const bool col_ok = c < a.D;
   const int chunk_rows = kRows * rpp;
   const long long cpb = (a.N + chunk_rows - 1) / chunk_rows;   // chunks per (b, h)
@@ -93,51 +95,62 @@ __global__ void __launch_bounds__(kThreads, 3) lse_merge_kernel(pa_merge_args a,
   for (long long ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
     const int bh = (int)(ch / cpb);
     const int row0 = (int)(ch - (long long)bh * cpb) * chunk_rows;
-    uint4 x1[kRows], x2[kRows];
+    const T* o1b = static_cast<const T*>(a.o1) + (long long)bh * a.o1_bh_stride + c;
+    const T* o2b = static_cast<const T*>(a.o2) + (long long)bh * a.o2_bh_stride + c;
+    T* ob = static_cast<T*>(a.o) + (long long)bh * a.o_bh_stride + c;
+    const float* l1b = a.lse1 + (long long)bh * a.lse1_bh_stride;
+    const float* l2b = a.lse2 + (long long)bh * a.lse2_bh_stride;
+    uint4 x1[kRows][kVecs], x2[kRows][kVecs];
     float l1[kRows], l2[kRows];
-    int rows[kRows];
 #pragma unroll
     for (int k = 0; k < kRows; ++k) {
       const int row = row0 + slot + k * rpp;
-      rows[k] = row;
       const bool in = row < a.N;
       const int r2 = !in ? -1 : (a.row_map2 ? a.row_map2[row] : row);
       const bool r2_ok = (unsigned)r2 < (unsigned)a.N;
-      l1[k] = in ? a.lse1[(long long)bh * a.lse1_bh_stride + row] : -INFINITY;
-      l2[k] = r2_ok ? a.lse2[(long long)bh * a.lse2_bh_stride + r2] : -INFINITY;
-      x1[k] = x2[k] = make_uint4(0u, 0u, 0u, 0u);
+      l1[k] = in ? l1b[row] : -INFINITY;
+      l2[k] = r2_ok ? l2b[r2] : -INFINITY;
+#pragma unroll
+      for (int v = 0; v < kVecs; ++v) x1[k][v] = x2[k][v] = make_uint4(0u, 0u, 0u, 0u);
       if (in && col_ok) {
-        const T* o1 = static_cast<const T*>(a.o1) + (long long)bh * a.o1_bh_stride +
-                      (long long)row * a.o1_row_stride + c;
-        x1[k] = *reinterpret_cast<const uint4*>(o1);
-        if (r2_ok) {
-          const T* o2 = static_cast<const T*>(a.o2) + (long long)bh * a.o2_bh_stride +
-                        (long long)r2 * a.o2_row_stride + c;
-          x2[k] = *reinterpret_cast<const uint4*>(o2);
+        const uint4* p1 = reinterpret_cast<const uint4*>(o1b + (long long)row * a.o1_row_stride);
+        const uint4* p2 = reinterpret_cast<const uint4*>(o2b + (long long)r2 * a.o2_row_stride);
+#pragma unroll
+        for (int v = 0; v < kVecs; ++v) {
+          if (c + 8 * v < a.D) {            // D a multiple of 8, not always of 16
+            x1[k][v] = p1[v];
+            if (r2_ok) x2[k][v] = p2[v];
+          }
         }
       }
     }
     float lse[kRows];
 #pragma unroll
     for (int k = 0; k < kRows; ++k) {
+      const int row = row0 + slot + k * rpp;
       float w1, w2;
       lse[k] = merge_weights(l1[k], l2[k], w1, w2);
-      if (rows[k] < a.N && col_ok) {
-        float f1[8], f2[8], y[8];
-        Vec8<T>::to_float(x1[k], f1);
-        Vec8<T>::to_float(x2[k], f2);
+      if (row < a.N && col_ok) {
+        uint4* po = reinterpret_cast<uint4*>(ob + (long long)row * a.o_row_stride);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = w1 * f1[i] + w2 * f2[i];
-        T* o = static_cast<T*>(a.o) + (long long)bh * a.o_bh_stride +
-               (long long)rows[k] * a.o_row_stride + c;
-        *reinterpret_cast<uint4*>(o) = Vec8<T>::from_float(y);
+        for (int v = 0; v < kVecs; ++v) {
+          if (c + 8 * v >= a.D) break;
+          float f1[8], f2[8], y[8];
+          Vec8<T>::to_float(x1[k][v], f1);
+          Vec8<T>::to_float(x2[k][v], f2);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) y[i] = w1 * f1[i] + w2 * f2[i];
+          po[v] = Vec8<T>::from_float(y);
+        }
       }
     }
     __syncwarp();   // every lane of these rows has read lse1 before it may be overwritten
     if (part == 0) {
 #pragma unroll
-      for (int k = 0; k < kRows; ++k)
-        if (rows[k] < a.N) a.lse[(long long)bh * a.lse_bh_stride + rows[k]] = lse[k];
+      for (int k = 0; k < kRows; ++k) {
+        const int row = row0 + slot + k * rpp;
+        if (row < a.N) a.lse[(long long)bh * a.lse_bh_stride + row] = lse[k];
+      }
     }
   }
 }
@@ -162,9 +175,9 @@ extern "C" int pa_lse_merge(const pa_merge_args* a, pa_stream_t stream) {
     PA_CHECK_ARG(s % 8 == 0, "pa_lse_merge: O strides must be multiples of 8 elements");
   PA_CHECK_ARG(aligned(a->o1, 16) && aligned(a->o2, 16) && aligned(a->o, 16),
                "pa_lse_merge: O pointers must be 16-byte aligned");
-  int tpr = a->D / 8;
+  int tpr = (a->D + 8 * kVecs - 1) / (8 * kVecs);   // threads per row, 16 columns each
   if (tpr > 32) tpr = 32;
-  while (kThreads % tpr) --tpr;
+  while (kThreads % tpr) ++tpr;                      // a power of two <= 32
   const long long chunk_rows = (long long)kRows * (kThreads / tpr);
   const long long nchunks = (a->N + chunk_rows - 1) / chunk_rows * a->BH;
   int dev = 0, sms = 148, per_sm = 4;

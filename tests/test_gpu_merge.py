@@ -10,7 +10,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [40, 64, 128])
 def test_lse_merge_matches_oracle(dtype, D):
     from polyhedral_b200 import merge
     BH, N = 3, 777
