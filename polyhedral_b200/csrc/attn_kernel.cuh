@@ -1021,8 +1021,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
                        : kRS          ? (row % P.nb) * P.rs + row / P.nb
                        : P.perm_q    ? __ldg(P.perm_q + row)
                                      : row;
-      // merge: the LSE in place is read now and the O row in place is pulled into
-      // L2, so the epilogue does not wait on memory for them
+      // merge: the LSE in place is read now (the O row in place is pulled into L2
+      // during the last super-tile), so the epilogue does not wait on memory for them
       float lse_prev = -INFINITY;
       if constexpr (kMerge) {
         if (valid) {
@@ -1030,10 +1030,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
                            : P.o_row_map ? __ldg(P.o_row_map + row)
                                          : row;
           if ((unsigned)orw0 < (unsigned)P.N) {
-            const char* op = static_cast<const char*>(P.o) +
-                             ((long long)bh * P.o_bh_stride + (long long)orw0 * P.o_row_stride) * 2;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(op));
-            if constexpr (D == 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(op + 128));
             asm volatile("ld.global.f32 %0, [%1];"
                          : "=f"(lse_prev)
                          : "l"(P.lse + (long long)bh * P.lse_bh_stride + orw0));
@@ -1043,6 +1039,22 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       float m_used = -INFINITY, l = 0.f;
       bool ok = true;
       for (int u = 0; u < nsup; ++u) {
+        if constexpr (kMerge) {
+          // the O row in place is pulled into L2 during the item's last super-tile,
+          // close enough to the epilogue to be still there (an item's K/V stream
+          // would have evicted it if fetched at the item's start)
+          if (u == nsup - 1 && valid) {
+            const int orw0 = kRS          ? (row % P.nb) * P.rs + row / P.nb
+                             : P.o_row_map ? __ldg(P.o_row_map + row)
+                                           : row;
+            if ((unsigned)orw0 < (unsigned)P.N) {
+              const char* op = static_cast<const char*>(P.o) +
+                               ((long long)bh * P.o_bh_stride + (long long)orw0 * P.o_row_stride) * 2;
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(op));
+              if constexpr (D == 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(op + 128));
+            }
+          }
+        }
         // this half's view of the super-tile's segments, from the plan descriptors
         int sts_[S], j0s[S], djs[S], shs[S], es[S], subs[S];
         bool aps[S];
@@ -1289,29 +1301,33 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           }
         }
       } else {
-        // merge: the rows in place are read through the staging buffer the same way
+        // merge: the rows in place are read through the staging buffer the same way;
+        // the loads of every 64-column chunk of the warp's 32 rows are issued before
+        // the first is used, so their round trips to memory overlap
         const int cc = lane & 7;
-#pragma unroll 1
+        uint4 ovs[D / 64][8];
+#pragma unroll
         for (int dh = 0; dh < D / 64; ++dh) {
-          // all eight loads are issued before the first shared-memory store, so the
-          // round trips to memory overlap
-          uint4 ov[8];
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int rr = it * 4 + (lane >> 3);
             const unsigned long long src =
                 __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(orow), rr);
-            ov[it] = make_uint4(0u, 0u, 0u, 0u);
+            ovs[dh][it] = make_uint4(0u, 0u, 0u, 0u);
             if (src)
               asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                           : "=r"(ov[it].x), "=r"(ov[it].y), "=r"(ov[it].z), "=r"(ov[it].w)
+                           : "=r"(ovs[dh][it].x), "=r"(ovs[dh][it].y), "=r"(ovs[dh][it].z),
+                             "=r"(ovs[dh][it].w)
                            : "l"(reinterpret_cast<const char*>(src) + dh * 128 + cc * 16));
           }
+        }
+#pragma unroll
+        for (int dh = 0; dh < D / 64; ++dh) {
           __syncwarp();   // the previous round's readers are done with the buffer
 #pragma unroll
           for (int it = 0; it < 8; ++it) {
             const int rr = it * 4 + (lane >> 3);
-            *reinterpret_cast<uint4*>(stage + rr * 128 + ((cc ^ (rr & 7)) << 4)) = ov[it];
+            *reinterpret_cast<uint4*>(stage + rr * 128 + ((cc ^ (rr & 7)) << 4)) = ovs[dh][it];
           }
           __syncwarp();
           uint32_t w[32];
