@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <math.h>
 #include <atomic>
+#include <cstring>
 #include <mutex>
 #include "attn_kernel.cuh"
 #include "attn_kernel_db.cuh"
@@ -375,6 +376,10 @@ int launch_fwd(const pa_attn_args* a, const PlanView& pv, cudaStream_t stream,
   PA_CHECK_ARG(aligned(a->o, 16) && a->o_row_stride % 8 == 0 && a->o_bh_stride % 8 == 0,
                "pa_attn_fwd: o must be 16-byte aligned with strides multiple of 8 elements");
   FwdParams P;
+  memset(&P.tm_o, 0, sizeof(P.tm_o));
+  if (!a->o_row_map && (rc = make_tmap(&P.tm_o, a->o, a->dtype, a->BH, a->N, a->D,
+                                       a->o_row_stride, a->o_bh_stride, 32, rs, "o")))
+    return rc;
   P.BH = a->BH;
   P.N = a->N;
   P.A = a->A;

@@ -99,6 +99,9 @@ inline int32_t launch_status(int32_t err_word, int32_t done_epoch) {
 // ------------------------------------------------------------- plan kernels
 // ------------------------------------------------------------- forward kernel
 struct FwdParams {
+  // O as a tensor map of boxes of 64 columns x 32 rows (one softmax warp's rows), for
+  // the epilogue's TMA loads (merge) and stores; unused when o_row_map scatters rows
+  CUtensorMap tm_o;
   int BH, N, A;
   int rs, nb;          // residue stride of a virtual permutation (0 = none), N / rs
   const int32_t* perm_q;
@@ -134,11 +137,14 @@ struct Smem {
   static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
   // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] drain item_full[2]
   //           item_empty[2] kv_full[S] kv_empty[S]
-  static constexpr int kNumBars = 15 + 2 * kSlots + (kCG == 2 ? 8 : 0);   // + pair_bar[8]
+  // kCG = 2: + pair_bar[8]; kCG = 1: + epi_bar[8] (a softmax warp's TMA load of the O
+  // rows in place, merge)
+  static constexpr int kNumBars = 15 + 2 * kSlots + 8;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
-  // kCG = 1: epilogue staging [8 warps][32 rows][128 B]; kCG = 2: no staging, and the
-  // row-max / row-sum exchange of the two threads of a row [2 halves][2 bufs][2][128]
-  static constexpr int kEpiOff = (kMiscOff + 32 + 127) & ~127;
+  // kCG = 1: epilogue staging [8 warps][32 rows][128 B], 128-byte swizzled boxes for the
+  // O tensor map (1024-byte aligned); kCG = 2: no staging, and the row-max / row-sum
+  // exchange of the two threads of a row [2 halves][2 bufs][2][128]
+  static constexpr int kEpiOff = (kMiscOff + 32 + 1023) & ~1023;
   static constexpr int kXchOff = kEpiOff;
   static constexpr int kBytes = kEpiOff + (kCG == 1 ? 8 * 32 * 128 : 2 * 2 * 2 * 128 * 4);
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
@@ -310,7 +316,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 template <int D, int L, bool kBf16, bool kRS, bool kMerge, bool kGather = false, int kCG = 1>
 __global__ void __launch_bounds__(Roles<kCG>::kThreads, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                const __grid_constant__ CUtensorMap tm_v, const FwdParams P) {
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ FwdParams P) {
   using SM = Smem<D, kCG>;
   using R = Roles<kCG>;
   constexpr int kLoadWarp = R::kLoadWarp;
@@ -336,6 +342,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint64_t* kv_full = bars + 15;
   uint64_t* kv_empty = bars + 15 + NS;
   uint64_t* pair_bar = bars + 15 + 2 * NS;   // kCG = 2: [half][lane quarter], 64 arrivals
+  uint64_t* epi_bar = bars + 15 + 2 * NS;    // kCG = 1: [softmax warp], TMA loads of old O
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
   volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
@@ -363,6 +370,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     }
     if constexpr (kCG == 2)
       for (int b = 0; b < 8; ++b) mbar_init(&pair_bar[b], 64);
+    else
+      for (int b = 0; b < 8; ++b) mbar_init(&epi_bar[b], 1);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -998,6 +1007,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     const uint32_t tS = tmem + lane_off + h * 128;
     const uint32_t tO = tmem + lane_off + 256 + h * D;
     uint32_t ts = 0, to = 0;
+    uint32_t epi_issued = 0, epi_done = 0;   // TMA loads of the staging (merge): issued, awaited
     const float c2 = P.scale_log2;
     uint32_t ring = 0;
     while (true) {
@@ -1251,11 +1261,111 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           }
         }
       }
-      // O leaves through a per-warp staging buffer so that every global store
-      // writes whole 128-byte row segments (8 lanes per row), including when rows
-      // are scattered by o_row_map; a merge reads the rows in place the same way.
+      // O leaves through the warp's staging buffer, 32 rows x 64 columns at a time.  Rows
+      // in the kernel's order (or, with the residue permutation, its original order) make
+      // one box of the O tensor map: the warp writes its rows into the 128-byte-swizzled
+      // staging and one lane stores the box with a TMA instruction (a merge first has the
+      // rows in place loaded into the same staging by TMA, and adds to them there).  Rows
+      // scattered by o_row_map are written lane by lane, whole 128-byte row segments at
+      // a time.
       uint8_t* stage = sEpi + warp * (32 * 128);
       const bool have_o = nsup > 0;
+      if (P.o_row_map == nullptr) {
+        const int wrow0 = p * 2 * BM + h * BM + wq * 32;   // the warp's first row
+        auto box_load = [&](int dh) {                       // lane 0, merge
+          mbar_arrive_expect_tx(&epi_bar[warp], 32 * 128);
+          if constexpr (kRS)
+            tma_load_4d(stage, &P.tm_o, &epi_bar[warp], dh * 64, wrow0 / P.nb, wrow0 % P.nb, bh);
+          else
+            tma_load_3d(stage, &P.tm_o, &epi_bar[warp], dh * 64, wrow0, bh);
+          ++epi_issued;
+        };
+        auto box_store = [&](int dh) {                      // lane 0
+          if constexpr (kRS)
+            tma_store_4d(&P.tm_o, stage, dh * 64, wrow0 / P.nb, wrow0 % P.nb, bh);
+          else
+            tma_store_3d(&P.tm_o, stage, dh * 64, wrow0, bh);
+          bulk_commit();
+        };
+        if constexpr (kMerge) {
+          if (lane == 0) {
+            bulk_wait_read();            // the warp's previous box store has read the staging
+            box_load(0);
+          }
+        }
+        if (have_o) {
+          ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
+          ++to;
+          if (!__all_sync(0xffffffffu, ok)) break;
+          tc_fence_after();
+        }
+#pragma unroll 1
+        for (int dh = 0; dh < D / 64; ++dh) {
+          uint32_t r0[32], r1[32];
+          if (have_o) {
+            tmem_ld32(tO + dh * 64, r0);
+            tmem_ld32(tO + dh * 64 + 32, r1);
+            tmem_wait_ld();
+            tmem_regs_ready(r0);
+            tmem_regs_ready(r1);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r0[i] = r1[i] = 0u;
+          }
+          if constexpr (kMerge) {
+            ok = mbar_wait(&epi_bar[warp], epi_done & 1, s_abort, err, DEV_TIMEOUT_O);
+            ++epi_done;
+            if (!__all_sync(0xffffffffu, ok)) break;
+            // this lane's row of the box: the row in place in, the merged row out
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint4* slot = reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4));
+              const uint4 v = *slot;
+              const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+              uint32_t w4[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int col = 8 * (c & 3) + 2 * j;
+                const float n0 = __uint_as_float(c < 4 ? r0[col] : r1[col]) * inv_l;
+                const float n1 = __uint_as_float(c < 4 ? r0[col + 1] : r1[col + 1]) * inv_l;
+                float a, b2;
+                unpack2<kBf16>(vv[j], a, b2);
+                w4[j] = pack2<kBf16>(fmaf(w_old, a, n0), fmaf(w_old, b2, n1));
+              }
+              *slot = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+          } else {
+            if (lane == 0) bulk_wait_read();   // the previous box store has read the staging
+            __syncwarp();
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint32_t w4[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int col = 8 * (c & 3) + 2 * j;
+                w4[j] = pack2<kBf16>(__uint_as_float(c < 4 ? r0[col] : r1[col]) * inv_l,
+                                     __uint_as_float(c < 4 ? r0[col + 1] : r1[col + 1]) * inv_l);
+              }
+              *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                  make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+          }
+          fence_proxy_async_shared();          // the rows are written before TMA reads them
+          __syncwarp();
+          if (lane == 0) {
+            box_store(dh);
+            if constexpr (kMerge) {
+              if (dh + 1 < D / 64) {
+                bulk_wait_read();
+                box_load(dh + 1);
+              }
+            }
+          }
+        }
+        if (!ok) break;
+        if (have_o) tc_fence_before();
+        continue;
+      }
       if (have_o) {
         ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
         ++to;
@@ -1374,6 +1484,18 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       }
       if (have_o) tc_fence_before();
     }
+    // the warp's TMA traffic of the staging is finished before the CTA can exit: a box
+    // load still in flight (an aborted merge) lands, every box store completes
+    if (lane == 0) {
+      if (epi_issued > epi_done) {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(&epi_bar[warp], (epi_issued - 1) & 1)) {
+          if (globaltimer() - t0 > kDrainLimitNs) { err.record(DEV_TIMEOUT_DRAIN); break; }
+        }
+      }
+      bulk_wait_all();
+    }
+    __syncwarp();
     }   // kCG == 1
   }
 

@@ -132,6 +132,29 @@ PA_DEV void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int c0, int 
         "r"(r3)
       : "memory");
 }
+// Tiled stores shared -> global (no multicast), completion tracked as a bulk group of
+// the issuing thread; the box is read from `src` (shared) laid out as the map's swizzle
+// says.  Never at a negative coordinate; c0 a multiple of 8 elements (16 bytes).
+PA_DEV void tma_store_3d(const void* tmap, const void* src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+      ::"l"(tmap), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2) : "memory");
+}
+PA_DEV void tma_store_4d(const void* tmap, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+      ::"l"(tmap), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3) : "memory");
+}
+PA_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Until every bulk group this thread committed has finished reading shared memory.
+PA_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Until every bulk group this thread committed has completed (written global memory).
+PA_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's ordinary shared-memory writes before later async-proxy (TMA)
+// accesses of them.
+PA_DEV void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 PA_DEV void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
