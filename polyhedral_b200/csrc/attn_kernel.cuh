@@ -137,16 +137,14 @@ struct Smem {
   static constexpr int kBarOff = kKVOff + kSlots * kTileBytes;
   // barriers: q_full[2] q_empty[2] s_full[2] p_full[2] o_full[2] drain item_full[2]
   //           item_empty[2] kv_full[S] kv_empty[S]
-  // kCG = 2: + pair_bar[8]; kCG = 1: + epi_bar[8] (a softmax warp's TMA load of the O
-  // rows in place, merge)
+  // kCG = 1: + epi_bar[8] (a softmax warp's TMA load of the O rows in place, merge)
   static constexpr int kNumBars = 15 + 2 * kSlots + 8;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
   // kCG = 1: epilogue staging [8 warps][32 rows][128 B], 128-byte swizzled boxes for the
-  // O tensor map (1024-byte aligned); kCG = 2: no staging, and the row-max / row-sum
-  // exchange of the two threads of a row [2 halves][2 bufs][2][128]
+  // O tensor map (1024-byte aligned); kCG = 2: none (the two threads of a row share a
+  // warp and exchange through shuffles)
   static constexpr int kEpiOff = (kMiscOff + 32 + 1023) & ~1023;
-  static constexpr int kXchOff = kEpiOff;
-  static constexpr int kBytes = kEpiOff + (kCG == 1 ? 8 * 32 * 128 : 2 * 2 * 2 * 128 * 4);
+  static constexpr int kBytes = kEpiOff + (kCG == 1 ? 8 * 32 * 128 : 0);
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
   // gathered K/V only: the landing place of the extra rows nobody reads (one
   // four-row gather: 4 rows x 128 bytes)
@@ -341,7 +339,6 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint64_t* item_empty = bars + 13;
   uint64_t* kv_full = bars + 15;
   uint64_t* kv_empty = bars + 15 + NS;
-  uint64_t* pair_bar = bars + 15 + 2 * NS;   // kCG = 2: [half][lane quarter], 64 arrivals
   uint64_t* epi_bar = bars + 15 + 2 * NS;    // kCG = 1: [softmax warp], TMA loads of old O
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
@@ -368,9 +365,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    if constexpr (kCG == 2)
-      for (int b = 0; b < 8; ++b) mbar_init(&pair_bar[b], 64);
-    else
+    if constexpr (kCG == 1)
       for (int b = 0; b < 8; ++b) mbar_init(&epi_bar[b], 1);
     *s_abort = 0;
     fence_barrier_init();
@@ -704,36 +699,22 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(R::kSoftmaxRegs));
     if constexpr (kCG == 2) {
       // ------------------------------------------------------------ softmax + epilogue,
-      // two threads per row: warp w of the 16 handles half h = w / 8, S columns
-      // [64 cg, 64 cg + 64) with cg = (w / 4) % 2, and TMEM lane quarter w % 4.  The two
-      // threads of a row combine their partial row maxima through shared memory and a
-      // 64-thread named barrier once per super-tile (so both make the same rescaling
-      // decisions), keep partial row sums, and each writes its half of the O row.  P
-      // columns [32 cg, 32 cg + 32) of the packed P overwrite S columns 64-127, which the
-      // partner has loaded before the barrier.
+      // two threads per row, in one warp: warp w of the 16 handles half h = w / 8 and the
+      // 16 TMEM lanes (query rows) 32 (w % 4) + 16 ((w / 4) % 2) + [0, 16); lane t takes
+      // row t % 16 of them and its S columns [64 cg, 64 cg + 64), cg = t / 16 (the
+      // .16x32bx2 TMEM shape).  The two threads of a row combine their partial row maxima
+      // by a shuffle once per super-tile (so both make the same rescaling decisions) and
+      // their partial row sums in the epilogue, and each writes its half of the O row.
+      // Columns [32 cg, 32 cg + 32) of the packed P overwrite S columns 64-127, which the
+      // partner lane loaded in the same warp-wide TMEM load.
       const int h = warp >> 3;
-      const int cg = (warp >> 2) & 1;
+      const int hs = (warp >> 2) & 1;
       const int wq = warp & 3;
-      const int r_in = wq * 32 + lane;
-      const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+      const int cg = lane >> 4;
+      const int r_in = wq * 32 + hs * 16 + (lane & 15);
+      const uint32_t lane_off = (uint32_t)(wq * 32 + hs * 16) << 16;
       const uint32_t tS = tmem + lane_off + h * 128;
-      const uint32_t tO = tmem + lane_off + 256 + h * D + cg * (D / 2);
-      float* xch = reinterpret_cast<float*>(smem + SM::kXchOff);
-      uint64_t* pbar = &pair_bar[h * 4 + wq];
-      uint32_t xb = 0;      // exchanges so far: buffer and barrier parity
-      // this thread's partial value in, the partner's out; the pair meets on an
-      // mbarrier (64 arrivals) whose wait is bounded like every other wait
-      auto exchange = [&](float mine, bool& ok) -> float {
-        float* base = xch + (h * 2 + (xb & 1)) * 2 * BM + r_in;
-        base[cg * BM] = mine;
-        tc_fence_before();     // this thread's TMEM loads before the partner's P stores
-        mbar_arrive(pbar);
-        ok = mbar_wait(pbar, xb & 1, s_abort, err, DEV_TIMEOUT_S) && ok;
-        tc_fence_after();
-        const float other = base[(cg ^ 1) * BM];
-        ++xb;
-        return other;
-      };
+      const uint32_t tO = tmem + lane_off + 256 + h * D;
       uint32_t ts = 0, to = 0;
       const float c2 = P.scale_log2;
       uint32_t ring = 0;
@@ -822,8 +803,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           float s[64];
           {
             uint32_t r0[32], r1[32];
-            tmem_ld32(tS + 64 * cg, r0);
-            tmem_ld32(tS + 64 * cg + 32, r1);
+            tmem_ld32_pair<64>(tS, r0);
+            tmem_ld32_pair<64>(tS + 32, r1);
             tmem_wait_ld();
             tmem_regs_ready(r0);
             tmem_regs_ready(r1);
@@ -853,8 +834,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
             }
             mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
           }
-          mx = fmaxf(mx, exchange(mx, ok));
-          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
           const float m_tile = mx * c2;
           const float m_new = fmaxf(m_used, m_tile);
           const float m_prev = m_used;
@@ -890,7 +870,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
               fadd2(r8[j], r8[j + 1], a, b);
               pk[i] = pack2<kBf16>(a, b);
             }
-            tmem_st16(tS + 64 + 32 * cg + q4 * 16, pk);
+            tmem_st16_pair<32>(tS + 64 + q4 * 16, pk);
           }
           l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
           // O rescale (rare), this thread's half of the row
@@ -899,12 +879,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
 #pragma unroll 1
             for (int k = 0; k < D / 64; ++k) {
               uint32_t r[32];
-              tmem_ld32(tO + k * 32, r);
+              tmem_ld32_pair<D / 2>(tO + k * 32, r);
               tmem_wait_ld();
               tmem_regs_ready(r);
 #pragma unroll
               for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-              tmem_st32(tO + k * 32, r);
+              tmem_st32_pair<D / 2>(tO + k * 32, r);
             }
           }
           tmem_wait_st();
@@ -913,8 +893,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         }
         if (!ok) break;
         // epilogue: the row's sum from both threads, O / l, LSE (written by cg 0)
-        l += exchange(l, ok);
-        if (!__all_sync(0xffffffffu, ok)) break;
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
         float inv_l = l > 0.f ? 1.f / l : 0.f;
         const float lse_v = l > 0.f ? (m_used + __log2f(l)) * 0.69314718055994530942f : -INFINITY;
         float w_old = 0.f;
@@ -959,7 +938,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         for (int k = 0; k < D / 64; ++k) {
           uint32_t r[32];
           if (have_o) {
-            tmem_ld32(tO + k * 32, r);
+            tmem_ld32_pair<D / 2>(tO + k * 32, r);
             tmem_wait_ld();
             tmem_regs_ready(r);
           } else {
