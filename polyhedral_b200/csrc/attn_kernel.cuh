@@ -22,7 +22,7 @@ constexpr int kMmaWarp = 9;
 // Warp roles of the forward kernel by column groups per row (kCG): with kCG = 1 one
 // softmax thread owns a row of S (8 softmax warps, the constants above); with kCG = 2
 // two threads share it, 64 columns each (16 softmax warps, 640 threads; setmaxnreg
-// split of the 640 x 96 launch registers: 512 x 96 + 128 x 88 = 60416; the split
+// split of the 640 x 96 launch registers: 512 x 104 + 128 x 64 = 61440; the split
 // with the fewest spills, ptxas -v).
 template <int kCG>
 struct Roles {
@@ -30,8 +30,8 @@ struct Roles {
   static constexpr int kThreads = kCG == 1 ? 384 : 640;
   static constexpr int kLoadWarp = kSoftmaxWarps;
   static constexpr int kMmaWarp = kSoftmaxWarps + 1;
-  static constexpr int kSoftmaxRegs = kCG == 1 ? 200 : 96;
-  static constexpr int kOtherRegs = kCG == 1 ? 104 : 88;
+  static constexpr int kSoftmaxRegs = kCG == 1 ? 200 : 104;
+  static constexpr int kOtherRegs = kCG == 1 ? 104 : 64;
 };
 constexpr int BM = 128;   // query rows per half
 constexpr int BN = 128;   // KV rows per super-tile
