@@ -1027,6 +1027,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       }
       float m_used = -INFINITY, l = 0.f;
       bool ok = true;
+      // the previous item's box stores have read the staging: waited for here, while
+      // the item's first S is still in flight, rather than in the epilogue
+      if (lane == 0) bulk_wait_read();
       for (int u = 0; u < nsup; ++u) {
         if constexpr (kMerge) {
           // the O row in place is pulled into L2 during the item's last super-tile,
@@ -1222,18 +1225,20 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
               // The row already holds the result (O1, l1) of a disjoint part:
               // O = (e^(l1-m) O1 + e^(l2-m) O2) / (e^(l1-m) + e^(l2-m)), m = max(l1, l2),
               // LSE = m + log(e^(l1-m) + e^(l2-m)); this part's weight folds into 1/l.
+              // (exponent and logarithm on the special-function unit: den is in [1, 2],
+              // so the approximations' error stays below 1e-6 of the LSE)
               const float lo = lse_prev;
               const float mm = fmaxf(lo, lse_v);
               float wa = 0.f, wb = 0.f;
               if (mm != -INFINITY) {
-                wa = expf(lo - mm);
-                wb = expf(lse_v - mm);
+                wa = ex2((lo - mm) * 1.44269504088896340736f);
+                wb = ex2((lse_v - mm) * 1.44269504088896340736f);
               }
               const float den = wa + wb;
-              const float inv = den > 0.f ? 1.f / den : 0.f;
+              const float inv = den > 0.f ? __fdividef(1.f, den) : 0.f;
               w_old = wa * inv;
               inv_l *= wb * inv;
-              *lp = den > 0.f ? mm + logf(den) : -INFINITY;
+              *lp = den > 0.f ? mm + __log2f(den) * 0.69314718055994530942f : -INFINITY;
             } else {
               *lp = lse_v;
             }
@@ -1267,10 +1272,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           bulk_commit();
         };
         if constexpr (kMerge) {
-          if (lane == 0) {
-            bulk_wait_read();            // the warp's previous box store has read the staging
-            box_load(0);
-          }
+          if (lane == 0) box_load(0);
         }
         if (have_o) {
           ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
@@ -1314,7 +1316,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
               *slot = make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
           } else {
-            if (lane == 0) bulk_wait_read();   // the previous box store has read the staging
+            if (lane == 0 && dh > 0) bulk_wait_read();   // the previous box store has read it
             __syncwarp();
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
