@@ -12,7 +12,10 @@
 // softmax -> P.V + next S -> softmax of the default kernel at the price of an N = 64
 // S-MMA (bounded by shared-memory reads of Q) and twice as many per-tile steps; it is
 // faster where per-tile mask work is heavy (many partial tiles), slower on mostly
-// full tiles.
+// full tiles.  Each half computes only the super-tiles live for it (the plan's
+// per-half status): a band narrower than the item's 256 rows leaves each half tiles
+// that only the other half needs, and skipping them gives the same result (a dead
+// tile adds exact zeros and never raises the running maximum).
 #pragma once
 #include "attn_kernel.cuh"
 
@@ -239,10 +242,11 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    // Per super-tile g (buffer b = g & 1): S_h(g) for both halves into S buffer b,
-    // then P_h(g-1).V(g-1) from buffer b ^ 1.  S(g + 1) therefore runs while the
-    // softmax warps work on S(g); S(g + 2) reuses buffer b only after P(g).V(g),
-    // which reads P from it, has been issued ahead of it in this thread's order.
+    // Per super-tile g: S_h(g) for each half h it is live for, into that half's S
+    // buffer gh[h] & 1 (gh[h] counts half h's live super-tiles), then the P.V of
+    // super-tile g - 1 for the halves live in it.  S_h(next) therefore runs while the
+    // softmax works on S_h(current); a buffer is rewritten only after the P.V that
+    // reads P from it has been issued ahead of it in this thread's order.
     if (lane == 0) {
       int qi = 0;
       uint32_t g = 0;                   // super-tiles issued so far (all items)
@@ -275,15 +279,31 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
           mma_ts(d, pa_ + kk * 8, vd + (uint64_t)((kk * 16 * 128) >> 4), P.idesc_pv,
                  (acc || kk > 0) ? 1u : 0u);
       };
-      // P.V of super-tile gp (both halves), accumulating unless it opens the item
-      auto pv_step = [&](uint32_t gp, bool acc) -> bool {
+      // whether any segment of super-tile u is live for half h
+      auto live_of = [&](const uint8_t* sts, int cnt, int u, int h) -> bool {
+        bool lv = false;
+#pragma unroll
+        for (int sg = 0; sg < S; ++sg) {
+          const int e = P.A <= BN ? u * S + sg : u / (P.A / BN);
+          if (e < cnt) lv |= ((__ldg(sts + e) >> (2 * h)) & 3u) != 0;
+        }
+        return lv;
+      };
+      // P.V of super-tile gp for the halves live in it (pd); pc = that tile's count
+      // among the half's live tiles, pacc = whether it accumulates (not the half's
+      // first live tile of the item)
+      uint32_t gh[2] = {0, 0};
+      auto pv_step = [&](uint32_t gp, const bool (&pd)[2], const uint32_t (&pc)[2],
+                         const bool (&pacc)[2]) -> bool {
         if (!wait_pos(2 * gp + 1)) return false;
-        const uint32_t vslot = (2 * gp + 1) % NS, b = gp & 1;
+        const uint32_t vslot = (2 * gp + 1) % NS;
         for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&p_full[h * 2 + b], (gp >> 1) & 1, s_abort, err, DEV_TIMEOUT_P))
+          if (!pd[h]) continue;
+          const uint32_t b = pc[h] & 1;
+          if (!mbar_wait(&p_full[h * 2 + b], (pc[h] >> 1) & 1, s_abort, err, DEV_TIMEOUT_P))
             return false;
           tc_fence_after();
-          issue_pv(h, vslot, b, acc);
+          issue_pv(h, vslot, b, pacc[h]);
           tc_commit(&pv_done[h]);
         }
         tc_commit(&kv_empty[vslot]);
@@ -300,25 +320,45 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         if (it < 0) break;
         int p, bh_unused;
         item_coords(P, it, p, bh_unused);
-        const int nsup = num_super64<L>(P, __ldg(P.pv.pair_cnt + p));
+        const int cnt = __ldg(P.pv.pair_cnt + p);
+        const int nsup = num_super64<L>(P, cnt);
         if (nsup == 0) continue;
+        const uint8_t* sts = P.pv.status + (size_t)p * P.pv.cap;
         ok = mbar_wait(&q_full[0], qi & 1, s_abort, P.err_q, DEV_TIMEOUT_Q) &&
              mbar_wait(&q_full[1], qi & 1, s_abort, P.err_q, DEV_TIMEOUT_Q);
         tc_fence_after();
         if (!ok) break;
+        bool pd[2] = {false, false}, pacc[2] = {false, false}, seen[2] = {false, false};
+        uint32_t pc[2] = {0, 0};
+        bool lv_next[2] = {live_of(sts, cnt, 0, 0), live_of(sts, cnt, 0, 1)};
         for (int u = 0; u < nsup && ok; ++u, ++g) {
+          const bool lv[2] = {lv_next[0], lv_next[1]};
+          if (u + 1 < nsup) {   // read a tile ahead, off the issue path
+            lv_next[0] = live_of(sts, cnt, u + 1, 0);
+            lv_next[1] = live_of(sts, cnt, u + 1, 1);
+          }
           if (!(ok = wait_pos(2 * g))) break;
           const uint32_t kslot = (2 * g) % NS;
           for (int h = 0; h < 2; ++h) {
-            issue_s(h, kslot, g & 1);
-            tc_commit(&s_full[h * 2 + (g & 1)]);
+            if (lv[h]) {
+              issue_s(h, kslot, gh[h] & 1);
+              tc_commit(&s_full[h * 2 + (gh[h] & 1)]);
+            }
             if (u == nsup - 1) tc_commit(&q_empty[h]);   // the item's last read of Q_h
           }
           tc_commit(&kv_empty[kslot]);
-          if (u > 0) ok = pv_step(g - 1, u > 1);
+          if (u > 0 && !(ok = pv_step(g - 1, pd, pc, pacc))) break;
+          for (int h = 0; h < 2; ++h) {
+            pd[h] = lv[h];
+            if (lv[h]) {
+              pc[h] = gh[h]++;
+              pacc[h] = seen[h];
+              seen[h] = true;
+            }
+          }
         }
         if (!ok) break;
-        if (!(ok = pv_step(g - 1, nsup > 1))) break;
+        if (!(ok = pv_step(g - 1, pd, pc, pacc))) break;
         for (int h = 0; h < 2; ++h) tc_commit(&o_full[h]);
         ++qi;
       }
@@ -339,7 +379,7 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + h * 128;   // + b * 64 for buffer b
     const uint32_t tO = tmem + lane_off + 256 + h * D;
-    uint32_t g = 0, to = 0;
+    uint32_t gh = 0, to = 0;             // this half's live super-tiles so far (all items)
     const float c2 = P.scale_log2;
     uint32_t ring = 0;
     while (true) {
@@ -381,9 +421,9 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
       for (int a = 0; a < kDescAhead; ++a) load_desc(a, dnext[a]);
       float m_used = -INFINITY, l = 0.f;
-      bool ok = true;
-      for (int u = 0; u < nsup; ++u, ++g) {
-        const uint32_t b = g & 1;
+      bool ok = true, first = true;        // first: no live super-tile yet in this item
+      for (int u = 0; u < nsup; ++u) {
+        const uint32_t b = gh & 1;
         uint2 dcur[S];
 #pragma unroll
         for (int sg = 0; sg < S; ++sg) dcur[sg] = dnext[0][sg];
@@ -392,6 +432,14 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
           for (int sg = 0; sg < S; ++sg) dnext[a][sg] = dnext[a + 1][sg];
         load_desc(u + kDescAhead, dnext[kDescAhead - 1]);
+        // a super-tile dead for this half is not computed for it (the MMA warp skips
+        // it from the same status bits)
+        {
+          bool live = false;
+#pragma unroll
+          for (int sg = 0; sg < S; ++sg) live |= ((dcur[sg].y >> (24 + 2 * h)) & 3u) != 0;
+          if (!live) continue;
+        }
         // live bits of this row for the tile's 64 columns
         uint32_t mk[2];
         {
@@ -426,7 +474,7 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
             mk[k] = w;
           }
         }
-        ok = mbar_wait(&s_full[h * 2 + b], (g >> 1) & 1, s_abort, err, DEV_TIMEOUT_S);
+        ok = mbar_wait(&s_full[h * 2 + b], (gh >> 1) & 1, s_abort, err, DEV_TIMEOUT_S);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
         float s[64];
@@ -467,7 +515,7 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         const float m_new = fmaxf(m_used, m_tile);
         bool bump = false;
         float factor = 1.f;
-        if (u == 0) {
+        if (first) {
           m_used = m_new;
         } else if (m_new > m_used + 8.0f) {
           bump = true;
@@ -500,7 +548,7 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         // O rescale (rare: only when the running max grew by more than 2^8).  The
         // previous tile's P.V may still be running: wait for it first.
         if (__any_sync(0xffffffffu, need_o)) {
-          ok = mbar_wait(&pv_done[h], (g - 1) & 1, s_abort, err, DEV_TIMEOUT_P);
+          ok = mbar_wait(&pv_done[h], (gh - 1) & 1, s_abort, err, DEV_TIMEOUT_P);
           if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
           tc_fence_after();
           const float f = need_o ? factor : 1.f;
@@ -518,6 +566,8 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[h * 2 + b]);
+        first = false;
+        ++gh;
       }
       if (!ok) break;
       // epilogue: O / l, LSE
@@ -538,6 +588,8 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       // writes whole 128-byte row segments (8 lanes per row), including when rows
       // are scattered by o_row_map.
       uint8_t* stage = sEpi + warp * (32 * 128);
+      // the MMA warp signals o_full for every item with super-tiles; O holds this
+      // half's result only if it had a live one
       const bool have_o = nsup > 0;
       if (have_o) {
         ok = mbar_wait(&o_full[h], to & 1, s_abort, err, DEV_TIMEOUT_O);
@@ -548,7 +600,7 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
       for (int dh = 0; dh < D / 64; ++dh) {
         uint32_t w[32];   // 64 outputs of this row, packed in pairs
-        if (have_o) {
+        if (have_o && !first) {
           uint32_t r0[32], r1[32];
           tmem_ld32(tO + dh * 64, r0);
           tmem_ld32(tO + dh * 64 + 32, r1);
