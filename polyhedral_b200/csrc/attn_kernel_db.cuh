@@ -40,7 +40,9 @@ struct Smem {
   //           item_full[2] item_empty[2] kv_full[S] kv_empty[S]
   static constexpr int kNumBars = 21 + 2 * kSlots;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
-  static constexpr int kEpiOff = (kMiscOff + 32 + 127) & ~127;   // [8 warps][32 rows][128 B]
+  // epilogue staging [8 warps][32 rows][128 B], 128-byte swizzled boxes for the O
+  // tensor map (1024-byte aligned)
+  static constexpr int kEpiOff = (kMiscOff + 32 + 1023) & ~1023;
   static constexpr int kBytes = kEpiOff + 8 * 32 * 128;
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
 };
@@ -75,7 +77,7 @@ __device__ __forceinline__ SegInfo64 seg_info64(const FwdParams& P, const int32_
 template <int D, int L, bool kBf16, bool kRS>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                const __grid_constant__ CUtensorMap tm_v, const FwdParams P) {
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ FwdParams P) {
   using SM = Smem<D>;
   constexpr int S = BN / L;              // segments per super-tile
   constexpr int NS = SM::kSlots;
@@ -422,6 +424,9 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       for (int a = 0; a < kDescAhead; ++a) load_desc(a, dnext[a]);
       float m_used = -INFINITY, l = 0.f;
       bool ok = true, first = true;        // first: no live super-tile yet in this item
+      // the previous item's box stores have read the staging: waited for here, while
+      // the item's first S is still in flight
+      if (lane == 0) bulk_wait_read();
       for (int u = 0; u < nsup; ++u) {
         const uint32_t b = gh & 1;
         uint2 dcur[S];
@@ -584,9 +589,11 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
           if (P.lse) P.lse[(long long)bh * P.lse_bh_stride + orw] = lse_v;
         }
       }
-      // O leaves through a per-warp staging buffer so that every global store
-      // writes whole 128-byte row segments (8 lanes per row), including when rows
-      // are scattered by o_row_map.
+      // O leaves through the warp's staging buffer, 32 rows x 64 columns at a time: the
+      // warp writes its rows into a 128-byte-swizzled box and one lane stores it with a
+      // TMA instruction through the O tensor map (rows in the kernel's order, or in
+      // original order through the residue view).  Rows scattered by o_row_map are
+      // written lane by lane, whole 128-byte row segments at a time.
       uint8_t* stage = sEpi + warp * (32 * 128);
       // the MMA warp signals o_full for every item with super-tiles; O holds this
       // half's result only if it had a live one
@@ -596,6 +603,48 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         ++to;
         if (!__all_sync(0xffffffffu, ok)) break;
         tc_fence_after();
+      }
+      if (P.o_row_map == nullptr) {
+        const int wrow0 = p * 2 * BM + h * BM + wq * 32;   // the warp's first row
+#pragma unroll 1
+        for (int dh = 0; dh < D / 64; ++dh) {
+          uint32_t r0[32], r1[32];
+          if (have_o && !first) {
+            tmem_ld32(tO + dh * 64, r0);
+            tmem_ld32(tO + dh * 64 + 32, r1);
+            tmem_wait_ld();
+            tmem_regs_ready(r0);
+            tmem_regs_ready(r1);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r0[i] = r1[i] = 0u;
+          }
+          if (lane == 0 && dh > 0) bulk_wait_read();   // the previous box store has read it
+          __syncwarp();
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col = 8 * (c & 3) + 2 * j;
+              w4[j] = pack2<kBf16>(__uint_as_float(c < 4 ? r0[col] : r1[col]) * inv_l,
+                                   __uint_as_float(c < 4 ? r0[col + 1] : r1[col + 1]) * inv_l);
+            }
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+          fence_proxy_async_shared();          // the rows are written before TMA reads them
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (kRS)
+              tma_store_4d(&P.tm_o, stage, dh * 64, wrow0 / P.nb, wrow0 % P.nb, bh);
+            else
+              tma_store_3d(&P.tm_o, stage, dh * 64, wrow0, bh);
+            bulk_commit();
+          }
+        }
+        if (have_o) tc_fence_before();
+        continue;
       }
 #pragma unroll
       for (int dh = 0; dh < D / 64; ++dh) {
@@ -639,6 +688,8 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   }
 
   // ------------------------------------------------------------ teardown
+  // every box store has completed before the CTA can exit
+  if (warp < 8 && lane == 0) bulk_wait_all();
   __syncwarp();
   tc_fence_before();
   __syncthreads();
