@@ -169,9 +169,10 @@ typedef struct pa_attn_args {
                                         the merge (src/polyattn/experiments/compose.py:7-17). */
   int32_t kv_rows;                   /* KV rows per super-tile of the forward: 0 or 128 (the
                                         default kernel), or 64 (S double-buffered in TMEM so
-                                        the next S runs during the softmax; faster where many
-                                        tiles are partial, e.g. lattice and sinks masks).  64
-                                        cannot be combined with merge. */
+                                        the next S runs during the softmax, and each 128-row
+                                        half computes only the tiles live for it; faster on
+                                        bands narrower than a 256-row item, e.g. a window of
+                                        64).  64 cannot be combined with merge. */
   /* The reference's class-B traffic emulation (gpu/triton_attn.py:99-128); all zero /
      one for the ordinary forward.  Same tiles, same predicate, same result: only the
      way K/V rows are fetched changes. */

@@ -21,9 +21,9 @@ directly; the block index is still that of the permuted mask); ``merge=True`` (w
 ``out`` and ``lse_out``) treats them as holding the result of an attention over a
 disjoint mask on the same rows and merges this one into them in the epilogue
 (log-sum-exp merge, as ``merge.lse_merge``), so a split runs without a merge pass;
-``kv_rows=64`` selects the 64-row super-tile kernel (S double-buffered in TMEM:
-faster where many tiles are partial, slower on mostly full tiles; not with
-``merge``).  ``sched_heads=G`` runs the work items in groups of G heads, one group
+``kv_rows=64`` selects the 64-row super-tile kernel (S double-buffered in TMEM, and
+each 128-row half computes only the tiles live for it: faster on bands narrower than
+an item's 256 rows, slower on mostly full tiles; not with ``merge``).  ``sched_heads=G`` runs the work items in groups of G heads, one group
 after another (default: all heads in one group); groups whose K/V fit in L2 cut DRAM
 re-reads when all heads' K/V do not.  ``row_threads=2`` splits every query row's
 softmax over two threads (64 columns each; not with ``merge``, ``kv_rows=64`` or
