@@ -88,14 +88,18 @@ def _peaks():
     return 1590.0, 1400.0, 6650.0, "fallback"
 
 
-def _traffic_from_profiles(workload):
-    """DRAM bytes per launch of the attention kernel from the committed ncu summary."""
+def _traffic_from_profiles(workload, part=None):
+    """DRAM bytes per launch of the attention kernel (of one part of a split) on the
+    full configuration, from the committed ncu summary."""
     p = ROOT / "profiles" / f"attn_fwd_{workload}.json"
     if p.exists():
         try:
-            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+            d = json.loads(p.read_text())
         except Exception:
             return None
+        if part is not None:
+            return (d.get("parts") or {}).get(part)
+        return d.get("dram_bytes_per_launch")
     return None
 
 
@@ -356,29 +360,41 @@ def run_ours(args, rank, world, device):
                    "note": "optional, not part of the step"}
 
     # dominant kernel alone, CUDA events on the launching stream (for a split: each
-    # part's launch alone, the dominant one by live work reported)
-    kernel_flops, kernel_name = flops_rank, "attn_fwd_kernel"
+    # part's launch alone, the one taking the most time reported, every part listed)
+    kernel_flops, kernel_name, kernel_part = flops_rank, "attn_fwd_kernel", None
     reps = max(min(args.steps, 200), 20)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def time_alone(run):
+        for i in range(3):
+            run(i)
+        e0.record()
+        for i in range(reps):
+            run(i)
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / reps
+
+    parts_line = None
     if pipe.split is not None:
         from polyhedral_b200 import masks_gpu
         part_flops = [4.0 * D * masks_gpu.numpy_mask(pn).live_count(N) * sh.size
                       for pn in pipe.split_names]
-        dom = max(range(len(part_flops)), key=lambda i: part_flops[i])
-        run_dom = lambda i: pipe.split.run_part(dom, *bufs[i % nbuf], *outs[i % nbuf])
-        kernel_flops = part_flops[dom]
-        kernel_name = f"attn_fwd_kernel ({pipe.split_names[dom]} part, merging)" if dom else \
-            f"attn_fwd_kernel ({pipe.split_names[dom]} part)"
+        part_ms = [time_alone(lambda i, k=k: pipe.split.run_part(k, *bufs[i % nbuf],
+                                                                  *outs[i % nbuf]))
+                   for k in range(len(part_flops))]
+        dom = max(range(len(part_ms)), key=lambda i: part_ms[i])
+        kernel_flops, kernel_ms, kernel_part = part_flops[dom], part_ms[dom], pipe.split_names[dom]
+        kernel_name = f"attn_fwd_kernel ({kernel_part} part, merging)" if dom else \
+            f"attn_fwd_kernel ({kernel_part} part)"
+        peak0 = _peaks()[0]
+        parts_line = [{"part": pn, "ms": round(ms, 5), "live_gflop": round(f / 1e9, 3),
+                       "tflops": round(f / (ms * 1e-3) / 1e12, 2),
+                       "frac": round(f / (ms * 1e-3) / 1e12 / peak0, 4),
+                       "merging": k > 0}
+                      for k, (pn, f, ms) in enumerate(zip(pipe.split_names, part_flops, part_ms))]
     else:
-        run_dom = lambda i: pipe.step(*bufs[i % nbuf], *outs[i % nbuf])
-    for i in range(3):
-        run_dom(i)
-    e0.record()
-    for i in range(reps):
-        run_dom(i)
-    e1.record()
-    torch.cuda.synchronize(device)
-    kernel_ms = e0.elapsed_time(e1) / reps
+        kernel_ms = time_alone(lambda i: pipe.step(*bufs[i % nbuf], *outs[i % nbuf]))
 
     _, _, hbm_peak, hbm_kind = _peaks()
     # the explicit class A gather (Q, K, V in one launch), HBM-bound
@@ -510,12 +526,14 @@ def run_ours(args, rank, world, device):
 
     peak, peak_sus, hbm, peak_kind = _peaks()
     ach = kernel_flops / (kernel_ms * 1e-3) / 1e12
-    traffic = _traffic_from_profiles(wl)
+    traffic = _traffic_from_profiles(wl, kernel_part)
     if traffic is not None and args.bh:
         traffic = None          # the committed figure is for the full configuration
+    elif traffic is not None:
+        traffic = int(traffic * sh.size / BH)   # this rank's share of the (b,h)
     roof = {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
             "frac": round(ach / peak, 4), "traffic": traffic,
-            "kernel": kernel_name, "kernel_ms": round(kernel_ms, 5),
+            "kernel": kernel_name, "kernel_ms": round(kernel_ms, 5), "parts": parts_line,
             "kernel_live_gflop": round(kernel_flops / 1e9, 3),
             "peak_source": f"{peak_kind} bf16 dense (burst), of measured"
                            if peak_kind == "measured" else "fallback bf16 dense"}
