@@ -128,6 +128,15 @@ struct FwdParams {
   int withhold_q;      // test hook: never load half 0's Q tile of a CTA's first item
 };
 
+// One entry of the work-item ring in shared memory, written by the producer before it
+// signals item_full: the item, its pair and (batch, head), the pair's list length and
+// the plan descriptors of the first super-tile's segments, so that the MMA and softmax
+// warps start an item without a chain of dependent global loads.
+struct ItemSlot {
+  int it, p, bh, cnt;
+  uint2 d0[2];   // kept when a super-tile has at most two segments
+};
+
 template <int D, int kCG = 1>
 struct Smem {
   static constexpr int kTileBytes = BM * D * 2;               // one 128-row tile, 16-bit
@@ -139,11 +148,12 @@ struct Smem {
   //           item_empty[2] kv_full[S] kv_empty[S]
   // kCG = 1: + epi_bar[8] (a softmax warp's TMA load of the O rows in place, merge)
   static constexpr int kNumBars = 15 + 2 * kSlots + 8;
-  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
+  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort
+  static constexpr int kSlotOff = kMiscOff + 16;               // item ring: ItemSlot[2]
   // kCG = 1: epilogue staging [8 warps][32 rows][128 B], 128-byte swizzled boxes for the
   // O tensor map (1024-byte aligned); kCG = 2: none (the two threads of a row share a
   // warp and exchange through shuffles)
-  static constexpr int kEpiOff = (kMiscOff + 32 + 1023) & ~1023;
+  static constexpr int kEpiOff = (kSlotOff + 2 * (int)sizeof(ItemSlot) + 1023) & ~1023;
   static constexpr int kBytes = kEpiOff + (kCG == 1 ? 8 * 32 * 128 : 0);
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
   // gathered K/V only: the landing place of the extra rows nobody reads (one
@@ -320,6 +330,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   constexpr int kLoadWarp = R::kLoadWarp;
   constexpr int kMmaWarp = R::kMmaWarp;
   constexpr int S = BN / L;              // segments per super-tile
+  // the ring entry carries the first super-tile's descriptors for one segment (more
+  // would cost the one-thread softmax registers it spills)
+  constexpr int kSlotSegs = 1;
   constexpr int NS = SM::kSlots;
   constexpr int kChunks = D / 64;        // 128-byte swizzle chunks along D
   constexpr uint32_t kRegion = BM * 128; // bytes of one 64-column chunk of a 128-row tile
@@ -342,7 +355,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint64_t* epi_bar = bars + 15 + 2 * NS;    // kCG = 1: [softmax warp], TMA loads of old O
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
-  volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
+  ItemSlot* s_slot = reinterpret_cast<ItemSlot*>(smem + SM::kSlotOff);   // [2]
   uint8_t* sEpi = smem + SM::kEpiOff;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -407,6 +420,25 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         }
       }
     };
+    // writes the ring entry of item `it` (or of the end marker, it < 0) into `sl`
+    auto fill_slot = [&](ItemSlot& sl, int it) {
+      sl.it = it;
+      if (it < 0) return;
+      int p, bh;
+      item_coords(P, it, p, bh);
+      const int cnt = __ldg(P.pv.pair_cnt + p);
+      sl.p = p;
+      sl.bh = bh;
+      sl.cnt = cnt;
+      if constexpr (S <= kSlotSegs) {
+        const uint2* desc = P.pv.desc + (size_t)p * P.pv.cap;
+#pragma unroll
+        for (int sg = 0; sg < S; ++sg) {
+          const int e = P.A <= BN ? sg : 0;
+          sl.d0[sg] = e < cnt ? __ldg(desc + e) : make_uint2(0u, 0u);
+        }
+      }
+    };
     if constexpr (kGather) {
       // Gathered K/V rows (the reference's GATHER_KV / GATHER_MULT knobs,
       // gpu/triton_attn.py:99-128): row j of the kernel order is read from row
@@ -441,7 +473,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
               !mbar_wait(&item_empty[rs], ((ring >> 1) - 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM)) {
             ok = 0;
           } else {
-            s_item[rs] = it;
+            fill_slot(s_slot[rs], it);
             mbar_arrive(&item_full[rs]);
           }
         }
@@ -531,13 +563,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         if (ring >= 2 &&
             !mbar_wait(&item_empty[rs], ((ring >> 1) - 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM))
           break;
-        s_item[rs] = it;
+        fill_slot(s_slot[rs], it);
         mbar_arrive(&item_full[rs]);
         ++ring;
         if (it < 0) break;
-        int p, bh;
-        item_coords(P, it, p, bh);
-        const int cnt = __ldg(P.pv.pair_cnt + p);
+        const int p = s_slot[rs].p, bh = s_slot[rs].bh, cnt = s_slot[rs].cnt;
         const int nsup = num_super<L>(P, cnt);
         if (nsup == 0) continue;
         const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
@@ -644,13 +674,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         const uint32_t rs = ring & 1;
         if (!(ok = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM)))
           break;
-        const int it = s_item[rs];
+        const int it = s_slot[rs].it, cnt = s_slot[rs].cnt;
         mbar_arrive(&item_empty[rs]);
         ++ring;
         if (it < 0) break;
-        int p, bh_unused;
-        item_coords(P, it, p, bh_unused);
-        const int nsup = num_super<L>(P, __ldg(P.pv.pair_cnt + p));
+        const int nsup = num_super<L>(P, cnt);
         if (nsup == 0) continue;
         ok = mbar_wait(&q_full[0], qi & 1, s_abort, P.err_q, DEV_TIMEOUT_Q) &&
              mbar_wait(&q_full[1], qi & 1, s_abort, P.err_q, DEV_TIMEOUT_Q);
@@ -722,14 +750,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         const uint32_t rs = ring & 1;
         bool got = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM);
         if (!__all_sync(0xffffffffu, got)) break;
-        const int it = s_item[rs];
+        const int it = s_slot[rs].it, p = s_slot[rs].p, bh = s_slot[rs].bh, cnt = s_slot[rs].cnt;
         __syncwarp();
         if (lane == 0) mbar_arrive(&item_empty[rs]);
         ++ring;
         if (it < 0) break;
-        int p, bh;
-        item_coords(P, it, p, bh);
-        const int cnt = __ldg(P.pv.pair_cnt + p);
         const int nsup = num_super<L>(P, cnt);
         const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
         const uint2* desc = P.pv.desc + (size_t)p * P.pv.cap;
@@ -993,14 +1018,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       const uint32_t rs = ring & 1;
       bool got = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM);
       if (!__all_sync(0xffffffffu, got)) break;
-      const int it = s_item[rs];
+      const int it = s_slot[rs].it, p = s_slot[rs].p, bh = s_slot[rs].bh, cnt = s_slot[rs].cnt;
+      uint2 d0[S];   // the first super-tile's descriptors, from the ring entry
+#pragma unroll
+      for (int sg = 0; sg < S; ++sg)
+        d0[sg] = S <= kSlotSegs ? s_slot[rs].d0[sg] : make_uint2(0u, 0u);
       __syncwarp();
       if (lane == 0) mbar_arrive(&item_empty[rs]);
       ++ring;
       if (it < 0) break;
-      int p, bh;
-      item_coords(P, it, p, bh);
-      const int cnt = __ldg(P.pv.pair_cnt + p);
       const int nsup = num_super<L>(P, cnt);
       const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
       const uint2* desc = P.pv.desc + (size_t)p * P.pv.cap;
@@ -1061,7 +1087,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
             sub = u - e * spt;
           }
           uint2 d = make_uint2(0u, 0u);
-          if (e < cnt) d = __ldg(desc + e);
+          if (S <= kSlotSegs && u == 0) d = d0[sg];
+          else if (e < cnt) d = __ldg(desc + e);
           sts_[sg] = (d.y >> (24 + 2 * h)) & 3;
           djs[sg] = (int)(d.y & 0xffffu);
           shs[sg] = (d.y & (1u << 20)) ? (int)((d.y >> 16) & 15u) : -1;

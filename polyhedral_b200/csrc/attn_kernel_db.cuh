@@ -39,10 +39,11 @@ struct Smem {
   // barriers: q_full[2] q_empty[2] s_full[2][2] p_full[2][2] pv_done[2] o_full[2] drain
   //           item_full[2] item_empty[2] kv_full[S] kv_empty[S]
   static constexpr int kNumBars = 21 + 2 * kSlots;
-  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort, item ring
+  static constexpr int kMiscOff = kBarOff + 8 * kNumBars;    // tmem base, abort
+  static constexpr int kSlotOff = kMiscOff + 16;               // item ring: ItemSlot[2]
   // epilogue staging [8 warps][32 rows][128 B], 128-byte swizzled boxes for the O
   // tensor map (1024-byte aligned)
-  static constexpr int kEpiOff = (kMiscOff + 32 + 1023) & ~1023;
+  static constexpr int kEpiOff = (kSlotOff + 2 * (int)sizeof(ItemSlot) + 1023) & ~1023;
   static constexpr int kBytes = kEpiOff + 8 * 32 * 128;
   static constexpr int kAlloc = kBytes + 1024;                 // room to align to 1024
 };
@@ -101,7 +102,7 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
   uint64_t* kv_empty = bars + 21 + NS;
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + SM::kMiscOff);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 4);
-  volatile int* s_item = reinterpret_cast<volatile int*>(smem + SM::kMiscOff + 8);   // [2]
+  ItemSlot* s_slot = reinterpret_cast<ItemSlot*>(smem + SM::kSlotOff);   // [2]
   uint8_t* sEpi = smem + SM::kEpiOff;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -159,17 +160,34 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         // fetch the next work item and hand it to the MMA and softmax warps
         int it = atomicAdd(P.pv.sched, 1);
         if (it >= P.total_items || *s_abort) it = -1;
+        // the ring entry: the item, its pair and (batch, head), the list length and the
+        // first super-tile's plan descriptors
         const uint32_t rs = ring & 1;
         if (ring >= 2 &&
             !mbar_wait(&item_empty[rs], ((ring >> 1) - 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM))
           break;
-        s_item[rs] = it;
+        ItemSlot& sl = s_slot[rs];
+        sl.it = it;
+        if (it >= 0) {
+          int pp, bb;
+          item_coords(P, it, pp, bb);
+          const int cc = __ldg(P.pv.pair_cnt + pp);
+          sl.p = pp;
+          sl.bh = bb;
+          sl.cnt = cc;
+          if constexpr (S <= 2) {
+            const uint2* desc = P.pv.desc + (size_t)pp * P.pv.cap;
+#pragma unroll
+            for (int sg = 0; sg < S; ++sg) {
+              const int e = P.A <= BN ? sg : 0;
+              sl.d0[sg] = e < cc ? __ldg(desc + e) : make_uint2(0u, 0u);
+            }
+          }
+        }
         mbar_arrive(&item_full[rs]);
         ++ring;
         if (it < 0) break;
-        int p, bh;
-        item_coords(P, it, p, bh);
-        const int cnt = __ldg(P.pv.pair_cnt + p);
+        const int p = sl.p, bh = sl.bh, cnt = sl.cnt;
         const int nsup = num_super64<L>(P, cnt);
         if (nsup == 0) continue;
         const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
@@ -316,13 +334,10 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         const uint32_t rs = ring & 1;
         if (!(ok = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM)))
           break;
-        const int it = s_item[rs];
+        const int it = s_slot[rs].it, p = s_slot[rs].p, cnt = s_slot[rs].cnt;
         mbar_arrive(&item_empty[rs]);
         ++ring;
         if (it < 0) break;
-        int p, bh_unused;
-        item_coords(P, it, p, bh_unused);
-        const int cnt = __ldg(P.pv.pair_cnt + p);
         const int nsup = num_super64<L>(P, cnt);
         if (nsup == 0) continue;
         const uint8_t* sts = P.pv.status + (size_t)p * P.pv.cap;
@@ -388,14 +403,14 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       const uint32_t rs = ring & 1;
       bool got = mbar_wait(&item_full[rs], (ring >> 1) & 1, s_abort, err, DEV_TIMEOUT_ITEM);
       if (!__all_sync(0xffffffffu, got)) break;
-      const int it = s_item[rs];
+      const int it = s_slot[rs].it, p = s_slot[rs].p, bh = s_slot[rs].bh, cnt = s_slot[rs].cnt;
+      uint2 d0[S];   // the first super-tile's descriptors, from the ring entry (S <= 2)
+#pragma unroll
+      for (int sg = 0; sg < S; ++sg) d0[sg] = S <= 2 ? s_slot[rs].d0[sg] : make_uint2(0u, 0u);
       __syncwarp();
       if (lane == 0) mbar_arrive(&item_empty[rs]);
       ++ring;
       if (it < 0) break;
-      int p, bh;
-      item_coords(P, it, p, bh);
-      const int cnt = __ldg(P.pv.pair_cnt + p);
       const int nsup = num_super64<L>(P, cnt);
       const int32_t* ent = P.pv.entries + (size_t)p * P.pv.cap;
       const uint2* desc = P.pv.desc + (size_t)p * P.pv.cap;
@@ -420,8 +435,14 @@ attn_fwd_db_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         }
       };
       uint2 dnext[kDescAhead][S];
+      if constexpr (S <= 2) {
 #pragma unroll
-      for (int a = 0; a < kDescAhead; ++a) load_desc(a, dnext[a]);
+        for (int sg = 0; sg < S; ++sg) dnext[0][sg] = d0[sg];
+      } else {
+        load_desc(0, dnext[0]);
+      }
+#pragma unroll
+      for (int a = 1; a < kDescAhead; ++a) load_desc(a, dnext[a]);
       float m_used = -INFINITY, l = 0.f;
       bool ok = true, first = true;        // first: no live super-tile yet in this item
       // the previous item's box stores have read the staging: waited for here, while
